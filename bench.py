@@ -1,0 +1,551 @@
+"""Benchmark of the hot path on B200: one JSON line per run.
+
+Default workload: FusedAddLayerNormFwdOp on x, residual
+(8192, 4096) bf16 ~ N(0, 1) with fp32 weight = 1 + 0.1 N(0,1), bias =
+0.1 N(0,1), eps 1e-5.  A step is one forward over that batch.  ``--op``
+selects another hot-path op at its BASELINE configuration (used for the
+per-op tables; the default line is the contract's headline).
+
+Metric: achieved HBM GB/s = algorithmic bytes of the op (its eval_roofline
+bytes) / time, summed over ranks (weak scaling: every rank runs its own
+batch, no collective on the data path).  MHA / GDN lines report TFLOP/s.
+
+Timing: W warm-up steps, then K steps bracketed by a barrier and
+``torch.cuda.synchronize()``, CUDA events on the launching stream around
+every step, max over ranks.  Inputs rotate over enough distinct buffer sets
+that every step's working set was evicted from the 126 MB L2 (the set count
+is in ``config``).  ``e2e`` repeats the measurement through the public op API
+with pinned HOST buffers: H2D of the inputs, the op, D2H of the outputs.
+
+``--impl reference`` times the reference's CPU path (the torch ref program,
+restated in ``oracle/``) on the host cores, rank 0 only.
+
+Run: python bench.py [--gpus N] [--steps K] [--warmup W] [--op NAME] [--impl ours|reference]
+(N > 1: python -m torch.distributed.run --nproc-per-node N bench.py --gpus N ...)
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from dataclasses import dataclass, field
+from pathlib import Path
+from typing import Callable, Optional
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "tile-ascendnpu-ops_b200"))
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+L2_BYTES = 126 * 1024 * 1024
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+# ----------------------------------------------------------------- workloads
+@dataclass
+class Workload:
+    """One op at one configuration."""
+
+    name: str
+    metric: str
+    unit: str  # "GB/s" or "TFLOP/s"
+    dtype: str
+    config: dict
+    make_inputs: Callable[[torch.device, int], tuple]  # (device, seed) -> device tensors
+    build_op: Callable[[], object]
+    run: Callable[[object, tuple], object]
+    work_per_step: Callable[[object], float]  # bytes (GB/s) or flops (TFLOP/s) per step
+    kernel_regex: str
+    cpu_fn: Optional[Callable[[tuple], object]] = None  # oracle on CPU tensors
+    cpu_slice: Optional[Callable[[tuple, int], tuple]] = None  # bounded sample of the inputs
+    cpu_units: Optional[Callable[[tuple], float]] = None  # work units of a sample
+    bound: str = "hbm"
+    extra: dict = field(default_factory=dict)
+
+
+def _faln() -> Workload:
+    from tileops.ops.norm import FusedAddLayerNormFwdOp
+
+    M, N = 8192, 4096
+
+    def make(dev, seed):
+        g = torch.Generator(device="cpu").manual_seed(seed)
+        x = torch.randn(M, N, generator=g).to(torch.bfloat16)
+        r = torch.randn(M, N, generator=g).to(torch.bfloat16)
+        w = 1.0 + 0.1 * torch.randn(N, generator=g)
+        b = 0.1 * torch.randn(N, generator=g)
+        return tuple(t.to(dev) for t in (x, r, w, b))
+
+    def units(inp):
+        m, n = inp[0].shape
+        return 4.0 * m * n * 2 + 2 * n * 4
+
+    def cpu(inp):
+        from oracle import reference as ref
+
+        return ref.fused_add_layer_norm(*inp)
+
+    return Workload(
+        name="fused_add_layer_norm", metric="achieved HBM GB/s (FusedAddLayerNormFwdOp)",
+        unit="GB/s", dtype="bf16",
+        config={"workload": "FusedAddLayerNormFwdOp x,residual (8192,4096) bf16 + fp32 "
+                            "weight/bias (N=4096), eps 1e-5 (BASELINE configs[1])",
+                "M": M, "N": N},
+        make_inputs=make, build_op=lambda: FusedAddLayerNormFwdOp(dtype=torch.bfloat16),
+        run=lambda op, inp: op(*inp), work_per_step=lambda op: float(op.eval_roofline()[1]),
+        kernel_regex="faln_rows", cpu_fn=cpu,
+        cpu_slice=lambda inp, rows: (inp[0][:rows], inp[1][:rows], inp[2], inp[3]),
+        cpu_units=units,
+    )
+
+
+def _gated(tanh: bool) -> Workload:
+    from tileops.ops.elementwise import GeluAndMulFwdOp, GeluTanhAndMulFwdOp
+
+    M, N = 4096, 11008
+    cls = GeluTanhAndMulFwdOp if tanh else GeluAndMulFwdOp
+
+    def make(dev, seed):
+        g = torch.Generator(device="cpu").manual_seed(seed)
+        return (torch.randn(M, 2 * N, generator=g).to(torch.bfloat16).to(dev),)
+
+    def cpu(inp):
+        from oracle import reference as ref
+
+        return (ref.gelu_tanh_and_mul if tanh else ref.gelu_and_mul)(inp[0])
+
+    name = "gelu_tanh_and_mul" if tanh else "gelu_and_mul"
+    return Workload(
+        name=name, metric=f"achieved HBM GB/s ({cls.__name__})", unit="GB/s", dtype="bf16",
+        config={"workload": f"{cls.__name__} x (4096, 22016) bf16 -> (4096, 11008) "
+                            "(BASELINE configs[0])", "M": M, "N": N},
+        make_inputs=make, build_op=lambda: cls(M, N, torch.bfloat16),
+        run=lambda op, inp: op(*inp), work_per_step=lambda op: float(op.eval_roofline()[1]),
+        kernel_regex="gated_vec", cpu_fn=cpu,
+        cpu_slice=lambda inp, rows: (inp[0][:rows],),
+        cpu_units=lambda inp: 3.0 * inp[0].shape[0] * (inp[0].shape[1] // 2) * 2,
+    )
+
+
+def _unary(kind: str) -> Workload:
+    from tileops.ops import elementwise as E
+
+    shape = (16384, 16384)
+    n = shape[0] * shape[1]
+    dtype = torch.int32 if kind == "bitwise_not" else torch.bfloat16
+    op_cls = {"hardswish": E.HardswishFwdOp, "hardsigmoid": E.HardsigmoidFwdOp,
+              "clamp_scalar": E.ClampScalarFwdOp, "isnan": E.IsnanFwdOp,
+              "isinf": E.IsinfFwdOp, "isfinite": E.IsfiniteFwdOp,
+              "bitwise_not": E.BitwiseNotFwdOp}[kind]
+
+    def build():
+        if kind == "clamp_scalar":
+            return op_cls(n, dtype, min=-0.5, max=0.5)
+        return op_cls(n, dtype)
+
+    def make(dev, seed):
+        g = torch.Generator(device="cpu").manual_seed(seed)
+        if dtype == torch.int32:
+            x = torch.randint(-128, 128, shape, generator=g, dtype=torch.int32)
+        else:
+            x = torch.randn(shape, generator=g).to(dtype)
+            if kind.startswith("is"):
+                q = n // 4
+                f = x.view(-1)
+                f[:q], f[q : 2 * q], f[2 * q : 3 * q] = float("nan"), float("inf"), float("-inf")
+        return (x.to(dev),)
+
+    def cpu(inp):
+        from oracle import reference as ref
+
+        fn = getattr(ref, kind)
+        return fn(inp[0], -0.5, 0.5) if kind == "clamp_scalar" else fn(inp[0])
+
+    out_b = 1 if kind.startswith("is") else dtype.itemsize
+    return Workload(
+        name=kind, metric=f"achieved HBM GB/s ({op_cls.__name__})", unit="GB/s",
+        dtype=str(dtype).split(".")[-1],
+        config={"workload": f"{op_cls.__name__} [16384, 16384] {str(dtype).split('.')[-1]}"},
+        make_inputs=make, build_op=build, run=lambda op, inp: op(*inp),
+        work_per_step=lambda op: float(op.eval_roofline()[1]),
+        kernel_regex="predicate_vec" if kind.startswith("is") else
+        ("xor_stream_vec" if kind == "bitwise_not" else "unary_map_vec"),
+        cpu_fn=cpu, cpu_slice=lambda inp, rows: (inp[0][:rows],),
+        cpu_units=lambda inp: float(inp[0].numel() * (dtype.itemsize + out_b)),
+    )
+
+
+def _causal_conv(activation) -> Workload:
+    from tileops.ops.convolution import CausalDepthwiseConv1dFwdOp
+
+    B, D, L, K = 8, 4096, 8192, 4
+
+    def make(dev, seed):
+        g = torch.Generator(device="cpu").manual_seed(seed)
+        x = torch.randn(B, D, L, generator=g).to(torch.bfloat16)
+        w = (0.5 * torch.randn(D, K, generator=g)).to(torch.bfloat16)
+        b = (0.1 * torch.randn(D, generator=g)).to(torch.bfloat16)
+        return tuple(t.to(dev) for t in (x, w, b))
+
+    def cpu(inp):
+        from oracle import reference as ref
+
+        return ref.causal_depthwise_conv1d(*inp, activation=activation)
+
+    return Workload(
+        name="causal_conv1d" + ("_silu" if activation else ""),
+        metric="achieved HBM GB/s (CausalDepthwiseConv1dFwdOp)", unit="GB/s", dtype="bf16",
+        config={"workload": f"causal depthwise conv1d x (8, 4096, 8192) bf16, w (4096, 4), "
+                            f"bias, left pad 3, activation={activation} (BASELINE configs[2])"},
+        make_inputs=make, build_op=lambda: CausalDepthwiseConv1dFwdOp(activation=activation),
+        run=lambda op, inp: op(*inp), work_per_step=lambda op: float(op.eval_roofline()[1]),
+        kernel_regex="dwconv_packet", cpu_fn=cpu,
+        cpu_slice=lambda inp, rows: (inp[0][:1, : max(rows // 64, 1)],
+                                     inp[1][: max(rows // 64, 1)], inp[2][: max(rows // 64, 1)]),
+        cpu_units=lambda inp: 2.0 * inp[0].numel() * 2 + inp[1].numel() * 2 + inp[2].numel() * 2,
+    )
+
+
+def workloads() -> dict[str, Callable[[], Workload]]:
+    table = {
+        "fused_add_layer_norm": _faln,
+        "gelu_and_mul": lambda: _gated(False),
+        "gelu_tanh_and_mul": lambda: _gated(True),
+        "causal_conv1d": lambda: _causal_conv(None),
+        "causal_conv1d_silu": lambda: _causal_conv("silu"),
+    }
+    for kind in ("hardswish", "hardsigmoid", "clamp_scalar", "isnan", "isinf", "isfinite",
+                 "bitwise_not"):
+        table[kind] = (lambda k: (lambda: _unary(k)))(kind)
+    return table
+
+
+# --------------------------------------------------------------- utilities
+def load_peaks() -> tuple[dict, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        try:
+            return json.loads(path.read_text()), "measured"
+        except ValueError:
+            pass
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def load_traffic(name: str) -> Optional[float]:
+    """DRAM bytes per launch of the op's dominant kernel from the committed ncu summary."""
+    path = ROOT / "profiles" / "ncu_traffic.json"
+    if not path.exists():
+        return None
+    try:
+        entry = json.loads(path.read_text()).get(name)
+    except ValueError:
+        return None
+    return None if entry is None else float(entry["bytes_per_launch"])
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML on a thread."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+        0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+        0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.005):
+        self.samples: list[tuple[int, int]] = []
+        self.max_mhz: Optional[int] = None
+        self.period = period_s
+        self._stop = threading.Event()
+        self._thread = None
+        self._handle = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            uuid = None
+            try:
+                uuid = torch.cuda.get_device_properties(device_index).uuid
+            except Exception:
+                pass
+            handle = None
+            if uuid is not None:
+                for i in range(pynvml.nvmlDeviceGetCount()):
+                    h = pynvml.nvmlDeviceGetHandleByIndex(i)
+                    if str(uuid) in str(pynvml.nvmlDeviceGetUUID(h)):
+                        handle = h
+            self._handle = handle or pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._handle, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._nvml = None
+
+    def _sample(self):
+        n = self._nvml
+        sm = n.nvmlDeviceGetClockInfo(self._handle, n.NVML_CLOCK_SM)
+        reasons = n.nvmlDeviceGetCurrentClocksEventReasons(self._handle)
+        self.samples.append((sm, reasons))
+
+    def _loop(self):
+        while not self._stop.is_set():
+            try:
+                self._sample()
+            except Exception:
+                return
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self._nvml is not None:
+            self._thread = threading.Thread(target=self._loop, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+            try:
+                self._sample()
+            except Exception:
+                pass
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"]}
+        busy = [s for s in self.samples if not (s[1] & 0x1)] or self.samples
+        reasons = set()
+        for _, r in busy:
+            for bit, name in self.REASONS.items():
+                if r & bit and bit != 0x1:
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(s[0] for s in busy), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(busy)}
+
+
+def dist_env() -> tuple[int, int, int]:
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)),
+            int(os.environ.get("WORLD_SIZE", 1)))
+
+
+def max_over_ranks(value: float, world: int, device) -> float:
+    if world == 1:
+        return value
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int, device) -> None:
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier(device_ids=[device.index])
+
+
+# ---------------------------------------------------------------- our arm
+def time_cpu_baseline(wl: Workload, budget_s: float = 8.0) -> dict:
+    """The oracle (the reference's torch CPU ref program) on a bounded sample."""
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    full = wl.make_inputs(torch.device("cpu"), 1235)
+    rows = 256
+    sample = wl.cpu_slice(full, rows)
+    wl.cpu_fn(sample)  # warm-up
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while time.perf_counter() < t_end or len(times) < 3:
+        t0 = time.perf_counter()
+        wl.cpu_fn(sample)
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    units = wl.cpu_units(sample)
+    value = units / med / (1e9 if wl.unit == "GB/s" else 1e12)
+    desc = ", ".join(f"{tuple(t.shape)}" for t in sample if isinstance(t, torch.Tensor))
+    return {"value": value, "unit": wl.unit, "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"oracle on inputs {desc}, median of {len(times)} reps ({med*1e3:.2f} ms)",
+            "cpu_count": os.cpu_count()}
+
+
+def run_ours(args, wl: Workload) -> Optional[dict]:
+    rank, local_rank, world = dist_env()
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=device)
+    op = wl.build_op()
+    probe = wl.make_inputs(device, 1235 + rank)
+    set_bytes = sum(t.numel() * t.element_size() for t in probe if isinstance(t, torch.Tensor))
+    out = wl.run(op, probe)
+    outs = out if isinstance(out, (tuple, list)) else (out,)
+    set_bytes += sum(t.numel() * t.element_size() for t in outs)
+    del out, outs
+    n_sets = max(2, min(8, -(-3 * L2_BYTES // max(set_bytes, 1)) + 1))
+    sets = [probe] + [wl.make_inputs(device, 1235 + rank + 1000 * i) for i in range(1, n_sets)]
+    work = wl.work_per_step(op)
+    stream = torch.cuda.current_stream(device)
+
+    for i in range(args.warmup):
+        wl.run(op, sets[i % n_sets])
+    torch.cuda.synchronize(device)
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    sampler = ClockSampler(local_rank)
+    barrier(world, device)
+    torch.cuda.synchronize(device)
+    with sampler:
+        for i in range(args.steps):
+            starts[i].record(stream)
+            wl.run(op, sets[i % n_sets])
+            ends[i].record(stream)
+        torch.cuda.synchronize(device)
+    barrier(world, device)
+    total_ms = starts[0].elapsed_time(ends[-1])
+    per_launch_ms = statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends))
+    total_ms = max_over_ranks(total_ms, world, device)
+    per_launch_ms = max_over_ranks(per_launch_ms, world, device)
+
+    # End to end through the public API with pinned host buffers.
+    host_in = [t.cpu().pin_memory() if isinstance(t, torch.Tensor) else t for t in sets[0]]
+    out = wl.run(op, sets[0])
+    outs = out if isinstance(out, (tuple, list)) else (out,)
+    host_out = [torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for o in outs]
+    h2d = sum(t.numel() * t.element_size() for t in host_in if isinstance(t, torch.Tensor))
+    d2h = sum(t.numel() * t.element_size() for t in host_out)
+    e2e_steps = max(3, min(args.steps, 30))
+
+    def e2e_step():
+        dev_in = [t.to(device, non_blocking=True) if isinstance(t, torch.Tensor) else t
+                  for t in host_in]
+        res = wl.run(op, tuple(dev_in))
+        res = res if isinstance(res, (tuple, list)) else (res,)
+        for h, d in zip(host_out, res):
+            h.copy_(d, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize(device)
+    barrier(world, device)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps, world, device)
+    barrier(world, device)
+
+    scale = 1e9 if wl.unit == "GB/s" else 1e12
+    value = world * work * args.steps / (total_ms * 1e-3) / scale
+    achieved = work / (per_launch_ms * 1e-3) / scale
+    peaks, peak_kind = load_peaks()
+    if wl.unit == "GB/s":
+        peak = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+        peak_unit = "GB/s"
+    else:
+        peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+        peak_unit = "TFLOP/s"
+    clocks = sampler.summary()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    if rank != 0:
+        return None
+    line = {
+        "metric": wl.metric, "value": value, "unit": wl.unit, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype,
+        "data": "synthetic (seeded torch.randn of the BASELINE shapes)",
+        "config": {**wl.config, "parallelism": f"independent batch per GPU x{world}",
+                   "l2": f"rotating {n_sets} input/output sets "
+                         f"({n_sets * set_bytes / 2**20:.0f} MiB) > 126 MB L2"},
+        "roofline": {"bound": wl.bound, "achieved": achieved, "peak": peak, "unit": peak_unit,
+                     "frac": achieved / peak, "traffic": load_traffic(wl.name),
+                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json)" if peak_kind ==
+                     "measured" else "fallback", "per_launch_ms": per_launch_ms,
+                     "algorithmic_per_launch": work},
+        "e2e": {"value": work / (e2e_ms * 1e-3) / scale, "unit": wl.unit,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
+                "api": f"{type(op).__name__}.__call__ with pinned host buffers"},
+        "gpu_launches": args.steps,
+        "clocks": clocks,
+    }
+    if world == 1 and not args.no_cpu_baseline and wl.cpu_fn is not None:
+        line["cpu_baseline"] = time_cpu_baseline(wl)
+    return line
+
+
+# ----------------------------------------------------------- reference arm
+def run_reference(args, wl: Workload) -> Optional[dict]:
+    rank, _, world = dist_env()
+    if rank != 0:
+        return None
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    full = wl.make_inputs(torch.device("cpu"), 1235)
+    rows = args.ref_rows
+    sample = wl.cpu_slice(full, rows)
+    for _ in range(args.warmup):
+        wl.cpu_fn(sample)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        wl.cpu_fn(sample)
+    sec = (time.perf_counter() - t0) / args.steps
+    scale = 1e9 if wl.unit == "GB/s" else 1e12
+    value = wl.cpu_units(sample) / sec / scale
+    desc = ", ".join(f"{tuple(t.shape)}" for t in sample if isinstance(t, torch.Tensor))
+    return {
+        "impl": "reference", "metric": wl.metric, "value": value, "unit": wl.unit,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": wl.dtype,
+        "data": "synthetic (seeded torch.randn of the BASELINE shapes)",
+        "config": {**wl.config, "parallelism": "host CPU, rank 0 only"},
+        "cpu_baseline": {"value": value, "unit": wl.unit, "cores": torch.get_num_threads(),
+                         "kind": "port",
+                         "sample": f"reference torch CPU ref program (restated in oracle/) on "
+                                   f"inputs {desc} per step"},
+        "e2e": {"value": value, "unit": wl.unit, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description="B200 TileOPs hot-path benchmark")
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--op", default="fused_add_layer_norm")
+    ap.add_argument("--ref-rows", type=int, default=256,
+                    help="rows of the batch the CPU reference processes per step")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    table = workloads()
+    if args.op not in table:
+        raise SystemExit(f"unknown --op {args.op}; choose from {sorted(table)}")
+    wl = table[args.op]()
+    line = run_reference(args, wl) if args.impl == "reference" else run_ours(args, wl)
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,155 @@
+/*
+ * tileops_c.h -- C ABI of the B200 (sm_100a) TileOPs forward-operator library.
+ *
+ * Every entry point takes plain device pointers, element counts / shapes and
+ * a CUDA stream handle passed as `void*` (a `cudaStream_t`; NULL selects the
+ * legacy default stream of the current context).  No entry point allocates
+ * device memory: the caller owns every input, output and workspace buffer.
+ * Kernels are enqueued on `stream` and the call returns without
+ * synchronising; a non-zero status is returned for invalid arguments (checked
+ * on the host before anything is enqueued) and for launch failures.
+ *
+ * Each entry point replaces one TileLang `@tilelang.jit(target="npuir")`
+ * factory of the reference (Yihuace/tile-ascendnpu-ops, package
+ * examples/TileOPs/tileops); the factory a function stands in for is named in
+ * its comment as file:line inside that package.
+ *
+ * Layout conventions: all tensors are dense and row-major (C-contiguous) in
+ * the shapes given.  Pointers passed to the vectorised paths should be
+ * 16-byte aligned; misaligned pointers take a scalar path (same results).
+ */
+#ifndef TILEOPS_C_H_
+#define TILEOPS_C_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define TILEOPS_OK 0
+#define TILEOPS_EBADDTYPE (-1) /* dtype code not supported by this entry   */
+#define TILEOPS_EBADSHAPE (-2) /* a size / shape argument is out of range   */
+#define TILEOPS_EALIGN (-3)    /* a pointer violates a hard alignment rule  */
+#define TILEOPS_ELAUNCH (-4)   /* the CUDA launch (or a CUDA call) failed   */
+#define TILEOPS_ETIMEOUT (-5)  /* a bounded device-side wait ran out        */
+#define TILEOPS_EINVAL (-6)    /* any other invalid argument (NULL pointer) */
+
+/* ---- dtype codes (torch dtype in parentheses) --------------------------- */
+#define TILEOPS_DT_F32 0  /* torch.float32  */
+#define TILEOPS_DT_F16 1  /* torch.float16  */
+#define TILEOPS_DT_BF16 2 /* torch.bfloat16 */
+#define TILEOPS_DT_BOOL 3 /* torch.bool (one byte, 0 or 1) */
+#define TILEOPS_DT_U8 4   /* torch.uint8    */
+#define TILEOPS_DT_I8 5   /* torch.int8     */
+#define TILEOPS_DT_I16 6  /* torch.int16    */
+#define TILEOPS_DT_I32 7  /* torch.int32    */
+#define TILEOPS_DT_I64 8  /* torch.int64    */
+
+/* ABI version of this header; bumped when a signature changes. */
+#define TILEOPS_ABI_VERSION 1
+
+int tileops_abi_version(void);
+/* Static, human-readable text for a status code. */
+const char* tileops_status_string(int status);
+/* Status of the last bounded device-side wait, read back by the host after
+ * the stream is synchronised (0 = every wait completed).  Used by the
+ * kernels that spin on an mbarrier (attention, gated delta net). */
+int tileops_device_error_flag(void* stream, int clear);
+
+/* ---- elementwise unary (flat, n elements; y may not alias x) ----------- */
+
+/* y = x * clamp(x + 3, 0, 6) / 6 in fp32, rounded once.  dtype f32/f16/bf16.
+ * Replaces hardswish_fwd_kernel,
+ * kernels/elementwise/hardswish/hardswish_kernel/hardswish_fwd_kernel.py:70. */
+int tileops_hardswish_fwd(const void* x, void* y, int64_t n, int dtype, void* stream);
+
+/* y = clamp(x + 3, 0, 6) / 6 in fp32 (NaN propagates).  dtype f32/f16/bf16.
+ * Replaces hardsigmoid_fwd_kernel,
+ * kernels/elementwise/hardsigmoid/hardsigmoid_kernel/perf_opt/hardsigmoid_fwd_kernel.py. */
+int tileops_hardsigmoid_fwd(const void* x, void* y, int64_t n, int dtype, void* stream);
+
+/* y = clamp(x, min, max) in fp32 with NaN propagation; a bound is applied
+ * only when its has_* flag is non-zero (at least one must be).  The bounds
+ * are rounded to fp32 first, as torch.clamp does for a float tensor.
+ * Replaces clamp_scalar_fwd_kernel,
+ * kernels/elementwise/clamp_scalar/clamp_scalar_kernel/perf_opt/clamp_scalar_fwd_kernel.py. */
+int tileops_clamp_scalar_fwd(const void* x, void* y, int64_t n, int dtype, int has_min,
+                             double min_val, int has_max, double max_val, void* stream);
+
+/* IEEE predicates, y is torch.bool (one byte per element, 0/1); x f32/f16/bf16.
+ * Replace isnan_fwd_kernel (kernels/elementwise/isnan/isnan_kernel/isnan_fwd_kernel.py),
+ * isinf_fwd_kernel (…/isinf/isinf_kernel/isinf_fwd_kernel.py) and
+ * isfinite_fwd_kernel (…/isfinite/isfinite_kernel/isfinite_fwd_kernel.py). */
+int tileops_isnan_fwd(const void* x, void* y, int64_t n, int dtype, void* stream);
+int tileops_isinf_fwd(const void* x, void* y, int64_t n, int dtype, void* stream);
+int tileops_isfinite_fwd(const void* x, void* y, int64_t n, int dtype, void* stream);
+
+/* y = ~x for u8/i8/i16/i32/i64, logical not for bool.
+ * Replaces bitwise_not_fwd_kernel,
+ * kernels/elementwise/bitwise_not/bitwise_not_kernel/bitwise_not_fwd_kernel.py. */
+int tileops_bitwise_not_fwd(const void* x, void* y, int64_t n, int dtype, void* stream);
+
+/* ---- gated activations: x is (M, 2N), y is (M, N) ---------------------- */
+
+/* y = 0.5*g*(1 + erf(g/sqrt(2))) * v, g = x[:, :N], v = x[:, N:], fp32 math.
+ * Replaces gelu_and_mul_fwd_kernel,
+ * kernels/elementwise/gelu_and_mul/gelu_and_mul_kernel/perf_opt/gelu_and_mul_fwd_kernel.py:143. */
+int tileops_gelu_and_mul_fwd(const void* x, void* y, int64_t M, int64_t N, int dtype,
+                             void* stream);
+
+/* y = 0.5*g*(1 + tanh(sqrt(2/pi)*(g + 0.044715 g^3))) * v, fp32 math.
+ * Replaces gelu_tanh_and_mul_fwd_kernel,
+ * kernels/elementwise/gelu_tanh_and_mul/gelu_tanh_and_mul_kernel/perf_opt/gelu_tanh_and_mul_fwd_kernel.py. */
+int tileops_gelu_tanh_and_mul_fwd(const void* x, void* y, int64_t M, int64_t N, int dtype,
+                                  void* stream);
+
+/* ---- fused residual add + LayerNorm ------------------------------------ */
+
+/* s = round_dtype(x + residual);  y = round_dtype((s - mean) * rstd * w + b)
+ * per row of N, statistics in fp32 (biased variance), rstd = 1/sqrt(var+eps).
+ * x, residual, y, residual_out: (M, N) of `dtype` (f32/f16/bf16).
+ * weight, bias: (N,) of `affine_dtype` (either `dtype` or f32).
+ * Replaces _fused_add_layer_norm_kernel,
+ * kernels/norm/fused_add_layer_norm/fused_add_layer_norm_kernel/_fused_add_layer_norm_kernel.py:144. */
+int tileops_fused_add_layer_norm_fwd(const void* x, const void* residual, const void* weight,
+                                     const void* bias, void* y, void* residual_out, int64_t M,
+                                     int64_t N, double eps, int dtype, int affine_dtype,
+                                     void* stream);
+
+/* ---- 1-D convolution (NCL) ---------------------------------------------- */
+
+#define TILEOPS_ACT_NONE 0
+#define TILEOPS_ACT_SILU 1
+
+/* Depthwise conv1d: out[n,c,l] = act(b[c] + sum_k w[c,k] * x[n,c,l*stride + k*dil - pad_left])
+ * with zero padding outside [0, l_in).  x (n, c, l_in), w (c, k) contiguous
+ * (the (c, 1, k) torch layout is the same memory), bias (c,) or NULL,
+ * y (n, c, l_out).  x/y `dtype` f16/bf16/f32; w/bias `w_dtype` (= dtype or f32).
+ * fp32 accumulation, one rounding.  Causal (Mamba-style) form: pad_left = k-1,
+ * l_out = l_in.
+ * Replaces _conv1d_direct_kernel,
+ * kernels/convolution/conv1d/conv1d_kernel/_conv1d_direct_kernel.py:163 (depthwise path
+ * selected by ops/convolution.py:143-145). */
+int tileops_conv1d_depthwise_fwd(const void* x, const void* w, const void* bias, void* y,
+                                 int64_t n, int64_t c, int64_t l_in, int64_t l_out,
+                                 int64_t k, int64_t stride, int64_t pad_left,
+                                 int64_t dilation, int dtype, int w_dtype, int activation,
+                                 void* stream);
+
+/* General grouped conv1d (any groups, stride, dilation, padding), fp32
+ * accumulation on CUDA cores: the dense/grouped conv1d kernels of the
+ * reference (kernels/convolution/conv1d/conv1d.py:152-516: pointwise, generic,
+ * unit-stride and group kernels).  x (n, c_in, l_in), w (c_out, c_in/groups, k),
+ * bias (c_out,) or NULL, y (n, c_out, l_out). */
+int tileops_conv1d_direct_fwd(const void* x, const void* w, const void* bias, void* y,
+                              int64_t n, int64_t c_in, int64_t l_in, int64_t c_out,
+                              int64_t l_out, int64_t k, int64_t stride, int64_t pad_left,
+                              int64_t dilation, int64_t groups, int dtype, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TILEOPS_C_H_ */

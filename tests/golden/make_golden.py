@@ -1,0 +1,295 @@
+"""Generate the golden fixtures from the reference implementation itself.
+
+Run in a checkout that has the reference (Yihuace/tile-ascendnpu-ops) next
+to it:
+
+    python tests/golden/make_golden.py --reference /path/to/tile-ascendnpu-ops
+
+The reference's op modules import the Ascend toolchain (torch_npu, TileLang
+npuir) at module level, so they cannot be imported here.  Its harness can
+(``tileops.workloads`` under ``examples/TileOPs`` imports on a CPU host), and
+its reference programs are plain torch.  This script therefore:
+
+1. draws every input with the reference's own workload classes on the CPU
+   after ``torch.manual_seed(1235)`` (the seed of the reference conftest,
+   examples/TileOPs/tests/conftest.py:10-12);
+2. extracts the reference programs from the reference source with ``ast``
+   (the ``ref_program`` method of each test class and the ``golden_*``
+   functions beside the kernels), compiles just those function bodies and
+   calls them -- the reference's own code computes every expected output;
+3. saves ``{inputs, outputs, meta}`` per case to ``tests/golden/<name>.pt``.
+
+Nothing in ``tests`` reads the reference at run time; only these fixtures.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ast
+import math
+import sys
+import types
+from math import sqrt
+from pathlib import Path
+
+import torch
+import torch.nn.functional as F
+
+HERE = Path(__file__).resolve().parent
+SEED = 1235
+
+
+class RefSource:
+    """Compile selected functions / methods out of reference source files."""
+
+    def __init__(self, root: Path):
+        self.root = root
+        self.to = root / "examples" / "TileOPs"
+
+    def _tree(self, rel: str) -> tuple[ast.Module, str]:
+        path = self.root / rel
+        text = path.read_text()
+        return ast.parse(text), text
+
+    def function(self, rel: str, name: str):
+        tree, _ = self._tree(rel)
+        for node in tree.body:
+            if isinstance(node, ast.FunctionDef) and node.name == name:
+                return self._compile(node, rel)
+        raise KeyError(f"{name} not found in {rel}")
+
+    def method(self, rel: str, cls: str, name: str):
+        tree, _ = self._tree(rel)
+        for node in tree.body:
+            if isinstance(node, ast.ClassDef) and node.name == cls:
+                for item in node.body:
+                    if isinstance(item, ast.FunctionDef) and item.name == name:
+                        return self._compile(item, rel)
+        raise KeyError(f"{cls}.{name} not found in {rel}")
+
+    @staticmethod
+    def _compile(node: ast.FunctionDef, rel: str):
+        node = ast.fix_missing_locations(node)
+        node.decorator_list = []
+        # Strip annotations: they may name types the namespace does not hold.
+        node.returns = None
+        for a in node.args.args + node.args.kwonlyargs:
+            a.annotation = None
+        mod = ast.Module(body=[node], type_ignores=[])
+        ns = {"torch": torch, "F": F, "math": math, "sqrt": sqrt}
+        exec(compile(mod, f"<reference {rel}>", "exec"), ns)
+        return ns[node.name]
+
+
+def save(name: str, inputs: dict, outputs: dict, meta: dict) -> None:
+    path = HERE / f"{name}.pt"
+    torch.save({"inputs": inputs, "outputs": outputs, "meta": meta}, path)
+    size = path.stat().st_size
+    print(f"  {path.name:48s} {size / 1024:8.1f} KiB")
+
+
+def corner_values(dtype: torch.dtype) -> torch.Tensor:
+    """IEEE corner inputs: signed zeros, +-1, +-3, +-6, extremes, +-inf, NaN, small values."""
+    fi = torch.finfo(dtype)
+    vals = [0.0, -0.0, 1.0, -1.0, 3.0, -3.0, 6.0, -6.0, 2.5, -2.5, fi.max, -fi.max, fi.tiny,
+            -fi.tiny, float("inf"), float("-inf"), float("nan"), 1.5, -2.25, 0.6931, -4.5,
+            4.5, 1e-4, -1e-4, 0.5, -0.5, 0.49, -0.51]
+    return torch.tensor(vals, dtype=dtype)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default="/root/reference", type=Path)
+    args = ap.parse_args()
+    src = RefSource(args.reference)
+    sys.path.insert(0, str(src.to))
+    from tileops.workloads.attention import MhaFwdWorkload
+    from tileops.workloads.convolution import Conv1dWorkload
+    from tileops.workloads.elementwise import (
+        BitwiseNotWorkload,
+        IsfiniteWorkload,
+        IsinfWorkload,
+        IsnanWorkload,
+    )
+    from tileops.workloads.norm import FusedAddLayerNormWorkload
+
+    T = "examples/TileOPs/tests/ops/"
+    K = "examples/TileOPs/tileops/kernels/"
+    dtypes = [torch.float32, torch.float16, torch.bfloat16]
+    dn = {torch.float32: "f32", torch.float16: "f16", torch.bfloat16: "bf16"}
+
+    # ---- unary float ops: ref_program of the reference tests ----
+    for op, rel, cls in [
+        ("hardswish", T + "test_hardswish.py", "HardswishTest"),
+        ("hardsigmoid", T + "test_hardsigmoid.py", "HardsigmoidTest"),
+    ]:
+        ref = src.method(rel, cls, "ref_program")
+        for dt in dtypes:
+            torch.manual_seed(SEED)
+            x = torch.cat([corner_values(dt), torch.randn(4096, dtype=dt)])
+            save(f"{op}_{dn[dt]}", {"x": x}, {"y": ref(None, x)},
+                 {"source": f"{rel}:{cls}.ref_program", "seed": SEED})
+
+    ref = src.method(T + "test_clamp_scalar.py", "ClampScalarTest", "ref_program")
+    for dt in dtypes:
+        for lo, hi, tag in [(-0.5, 0.5, "both"), (None, 0.5, "max"), (-0.5, None, "min")]:
+            torch.manual_seed(SEED)
+            x = torch.cat([corner_values(dt), torch.randn(4096, dtype=dt)])
+            self_ = types.SimpleNamespace(min_val=lo, max_val=hi)
+            save(f"clamp_scalar_{tag}_{dn[dt]}", {"x": x}, {"y": ref(self_, x)},
+                 {"source": "test_clamp_scalar.py:ClampScalarTest.ref_program", "min": lo,
+                  "max": hi, "seed": SEED})
+    ref = src.method(T + "test_clamp_min.py", "ClampMinTest", "ref_program")
+    for dt in dtypes:
+        torch.manual_seed(SEED)
+        x = torch.cat([corner_values(dt), torch.randn(4096, dtype=dt)])
+        save(f"clamp_min_{dn[dt]}", {"x": x},
+             {"y": ref(types.SimpleNamespace(min_val=-0.5), x)},
+             {"source": "test_clamp_min.py:ClampMinTest.ref_program", "min": -0.5, "seed": SEED})
+
+    # ---- predicates: the reference special-value workload + ref_program ----
+    for op, wl, rel, cls in [
+        ("isnan", IsnanWorkload, T + "test_isnan.py", "IsnanTest"),
+        ("isinf", IsinfWorkload, T + "test_isinf.py", "IsinfTest"),
+        ("isfinite", IsfiniteWorkload, T + "test_isfinite.py", "IsfiniteTest"),
+    ]:
+        ref = src.method(rel, cls, "ref_program")
+        for dt in dtypes:
+            torch.manual_seed(SEED)
+            (x,) = wl((4099,), dt).gen_inputs()
+            x = torch.cat([x, corner_values(dt)])
+            save(f"{op}_{dn[dt]}", {"x": x}, {"y": ref(None, x)},
+                 {"source": f"{rel}:{cls}.ref_program", "seed": SEED})
+
+    # ---- bitwise not ----
+    ref = src.method(T + "test_bitwise_not.py", "BitwiseNotTest", "ref_program")
+    for dt in [torch.bool, torch.uint8, torch.int8, torch.int16, torch.int32, torch.int64]:
+        torch.manual_seed(SEED)
+        (x,) = BitwiseNotWorkload((4101,), dt).gen_inputs()
+        if dt not in (torch.bool,):
+            info = torch.iinfo(dt)
+            x = torch.cat([x, torch.tensor([info.min, info.max, 0, -1 if info.min < 0 else 1],
+                                           dtype=dt)])
+        save(f"bitwise_not_{str(dt).split('.')[-1]}", {"x": x}, {"y": ref(None, x)},
+             {"source": "test_bitwise_not.py:BitwiseNotTest.ref_program", "seed": SEED})
+
+    # ---- gated ops: reference smoke shape (16, 128) plus corner gates ----
+    for op, rel, cls in [
+        ("gelu_and_mul", T + "test_gelu_and_mul.py", "GeluAndMulTest"),
+        ("gelu_tanh_and_mul", T + "test_gelu_tanh_and_mul.py", "GeluTanhAndMulTest"),
+    ]:
+        ref = src.method(rel, cls, "ref_program")
+        for dt in dtypes:
+            torch.manual_seed(SEED)
+            x = torch.randn(16, 256, dtype=dt)
+            c = corner_values(dt)
+            x[0, : c.numel()] = c  # gates
+            x[1, 128 : 128 + c.numel()] = c  # values
+            save(f"{op}_{dn[dt]}", {"x": x}, {"y": ref(None, x)},
+                 {"source": f"{rel}:{cls}.ref_program", "M": 16, "N": 128, "seed": SEED})
+    gold = src.function(K + "elementwise/gelu_and_mul/gelu_and_mul_kernel/perf_opt/"
+                        "gelu_and_mul_fwd_kernel.py", "golden_gelu_and_mul")
+    torch.manual_seed(SEED)
+    x = torch.randn(8, 64, dtype=torch.float32)
+    save("gelu_and_mul_golden_f32", {"x": x}, {"y": gold(x)},
+         {"source": "gelu_and_mul_fwd_kernel.py:golden_gelu_and_mul", "M": 8, "N": 32})
+
+    # ---- fused add layer norm: reference workload + ref_program ----
+    ref = src.method(T + "test_fused_add_layer_norm.py", "FusedAddLayerNormTest", "ref_program")
+    for m, n, dt in [(4, 4096, torch.float32), (4, 4096, torch.float16),
+                     (4, 4096, torch.bfloat16), (16, 1152, torch.float16),
+                     (2, 5120, torch.float32), (3, 1000, torch.bfloat16)]:
+        torch.manual_seed(SEED)
+        wl = FusedAddLayerNormWorkload(m, n, dt)
+        x, r, w, b = wl.gen_inputs()
+        y, added = ref(types.SimpleNamespace(n=n, eps=wl.eps), x, r, w, b)
+        save(f"fused_add_layer_norm_{m}x{n}_{dn[dt]}", {"x": x, "residual": r, "weight": w,
+             "bias": b}, {"y": y, "residual_out": added},
+             {"source": "test_fused_add_layer_norm.py:FusedAddLayerNormTest.ref_program",
+              "eps": wl.eps, "seed": SEED})
+    gold = src.function(K + "norm/fused_add_layer_norm/fused_add_layer_norm_kernel/"
+                        "_fused_add_layer_norm_kernel.py", "golden_fused_add_layer_norm")
+    torch.manual_seed(SEED)
+    x, r, w, b = FusedAddLayerNormWorkload(4, 512, torch.bfloat16).gen_inputs()
+    y, added = gold(x, r, w, b, 1e-5)
+    save("fused_add_layer_norm_golden_bf16", {"x": x, "residual": r, "weight": w, "bias": b},
+         {"y": y, "residual_out": added},
+         {"source": "_fused_add_layer_norm_kernel.py:golden_fused_add_layer_norm", "eps": 1e-5})
+
+    # ---- conv1d: reference Conv1dWorkload (gen_inputs + ref_program) ----
+    cases = [
+        ("tcn_k3_f16", (1, 32, 256, 64, 3, 1, 1, 1, 1, torch.float16, False)),
+        ("pad_wider_than_row_f16", (1, 17, 5, 7, 3, 1, 5, 2, 1, torch.float16, False)),
+        ("depthwise_k3_f16", (1, 32, 128, 32, 3, 1, 1, 1, 32, torch.float16, False)),
+        ("depthwise_k31_bias_f16", (1, 64, 128, 64, 31, 1, 15, 1, 64, torch.float16, True)),
+        ("depthwise_k4_bias_bf16", (2, 16, 256, 16, 4, 1, 3, 1, 16, torch.bfloat16, True)),
+        ("groups2_k3_f16", (1, 32, 128, 64, 3, 1, 1, 1, 2, torch.float16, False)),
+        ("same_k2_f16", (1, 16, 129, 32, 2, 1, "same", 1, 1, torch.float16, False)),
+        ("stride2_k5_f16", (1, 8, 100, 16, 5, 2, 2, 1, 1, torch.float16, False)),
+    ]
+    for tag, params in cases:
+        torch.manual_seed(SEED)
+        wl = Conv1dWorkload(*params)
+        x, w, b = wl.gen_inputs()
+        if b is not None:
+            b = torch.randn_like(b)  # a non-zero bias exercises the bias path
+        y = wl.ref_program(x, w, b)
+        names = ("n c_in l_in c_out kernel_size stride padding dilation groups dtype "
+                 "use_bias").split()
+        save(f"conv1d_{tag}", {"x": x, "weight": w, "bias": b}, {"y": y},
+             {"source": "workloads/convolution.py:Conv1dWorkload.ref_program",
+              **{k: v for k, v in zip(names, params)}})
+    gold = src.function(K + "convolution/conv1d/conv1d_kernel/_conv1d_direct_kernel.py",
+                        "golden_conv1d_depthwise")
+    torch.manual_seed(SEED)
+    x = torch.randn(2, 24, 200, dtype=torch.bfloat16)
+    w = (0.5 * torch.randn(24, 1, 4)).to(torch.bfloat16)
+    b = (0.1 * torch.randn(24)).to(torch.bfloat16)
+    y = gold(x, w, b, stride=1, padding=3, dilation=1)
+    save("conv1d_depthwise_golden_causal_bf16", {"x": x, "weight": w, "bias": b},
+         {"y_full": y},
+         {"source": "_conv1d_direct_kernel.py:golden_conv1d_depthwise", "padding": 3,
+          "note": "both-side padding 3; the causal output is y_full[..., :L]"})
+
+    # ---- attention: reference MhaFwdWorkload + SDPA ref_program + lse golden ----
+    ref = src.method(T + "test_multi_head_attention.py", "MhaFwdTest", "ref_program")
+    gold = src.function(K + "attention/multi_head_attention/multi_head_attention_kernel/"
+                        "perf_opt/_gqa_prefill_fwd_kernel.py", "golden_gqa_prefill_fwd")
+    for b_, s_, h_, d_, causal, dt in [(1, 128, 2, 64, False, torch.float16),
+                                       (1, 128, 2, 64, True, torch.bfloat16),
+                                       (1, 192, 1, 128, True, torch.bfloat16),
+                                       (1, 256, 1, 128, False, torch.bfloat16)]:
+        torch.manual_seed(SEED)
+        wl = MhaFwdWorkload(b_, h_, s_, d_, causal, dt)
+        q, k, v = wl.gen_inputs()
+        o_sdpa, _ = ref(types.SimpleNamespace(is_causal=causal), q, k, v)
+        o_gold, lse = gold(q, k, v, causal)
+        save(f"mha_b{b_}_s{s_}_h{h_}_d{d_}_{'causal' if causal else 'full'}_{dn[dt]}",
+             {"q": q, "k": k, "v": v}, {"o_sdpa": o_sdpa, "o_golden": o_gold, "lse": lse},
+             {"source": "test_multi_head_attention.py:MhaFwdTest.ref_program + "
+                        "_gqa_prefill_fwd_kernel.py:golden_gqa_prefill_fwd",
+              "is_causal": causal, "seed": SEED})
+
+    # ---- GDN: the probe's sequential golden on the probe's own cases ----
+    gold = src.function("examples/gdn_prefill/probe/gdn_prefill_probe.py",
+                        "golden_gdn_sequential")
+    probe_cases = [(1, 2, 48, 16, 16), (2, 1, 48, 16, 16), (1, 1, 64, 32, 32),
+                   (1, 1, 192, 64, 64), (1, 1, 130, 128, 128)]
+    for bb, hh, tt, dd, dvv in probe_cases:
+        torch.manual_seed(0)  # the probe's seed (gdn_prefill_probe.py:_run_case)
+        scale = dd**-0.5
+        q = (torch.randn(bb, hh, tt, dd) * 0.5).to(torch.float16)
+        k = (torch.randn(bb, hh, tt, dd) * 0.5).to(torch.float16)
+        v = (torch.randn(bb, hh, tt, dvv) * 0.5).to(torch.float16)
+        g = (-torch.rand(bb, hh, tt) * 0.3).to(torch.float16)
+        beta = torch.rand(bb, hh, tt).to(torch.float16)
+        s0 = torch.randn(bb, hh, dd, dvv, dtype=torch.float32) * 0.1
+        o, s = gold(q, k, v, g, beta, s0, scale)
+        save(f"gdn_b{bb}_h{hh}_t{tt}_d{dd}_dv{dvv}", {"q": q, "k": k, "v": v, "g": g,
+             "beta": beta, "state0": s0}, {"o": o, "final_state": s},
+             {"source": "gdn_prefill_probe.py:golden_gdn_sequential", "layout": "BHTD",
+              "scale": scale, "seed": 0})
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,92 @@
+"""The C-ABI library: it loads, exports every function the header declares,
+and rejects invalid arguments on the host before touching the GPU.  CPU only
+(every call here fails argument validation before any CUDA call)."""
+
+import ctypes
+
+import pytest
+
+from tileops import _native
+
+NULL = ctypes.c_void_p(0)
+
+
+def test_library_loads():
+    assert _native.LIB_PATH.exists(), "run __graft_entry__.build() first"
+    assert _native.lib().tileops_abi_version() == 1
+
+
+def test_every_declared_entry_point_is_exported():
+    declared = _native.declared_entry_points()
+    assert len(declared) >= 15
+    handle = _native.lib()
+    missing = [name for name in declared if not hasattr(handle, name)]
+    assert not missing, f"declared in include/tileops_c.h but not exported: {missing}"
+
+
+def test_every_declared_entry_point_has_a_python_signature():
+    assert set(_native.declared_entry_points()) <= set(_native._SIGNATURES)
+
+
+def test_status_strings():
+    lib = _native.lib()
+    for code in (0, -1, -2, -3, -4, -5, -6):
+        assert lib.tileops_status_string(code)
+    assert lib.tileops_status_string(0) == b"ok"
+    assert lib.tileops_status_string(-99) == b"unknown status"
+
+
+@pytest.mark.parametrize(
+    "name",
+    ["tileops_hardswish_fwd", "tileops_hardsigmoid_fwd", "tileops_isnan_fwd",
+     "tileops_isinf_fwd", "tileops_isfinite_fwd", "tileops_bitwise_not_fwd"],
+)
+def test_unary_rejects_negative_size(name):
+    assert getattr(_native.lib(), name)(NULL, NULL, -1, 0, NULL) == _native.EBADSHAPE
+
+
+@pytest.mark.parametrize("name", ["tileops_hardswish_fwd", "tileops_isnan_fwd"])
+def test_unary_empty_is_ok_and_null_is_rejected(name):
+    lib = _native.lib()
+    assert getattr(lib, name)(NULL, NULL, 0, 0, NULL) == _native.OK
+    assert getattr(lib, name)(NULL, NULL, 16, 0, NULL) == _native.EINVAL
+
+
+def test_bitwise_not_rejects_float_dtype():
+    assert _native.lib().tileops_bitwise_not_fwd(NULL, NULL, 16, 0, NULL) == _native.EBADDTYPE
+
+
+def test_clamp_requires_a_bound():
+    r = _native.lib().tileops_clamp_scalar_fwd(NULL, NULL, 16, 0, 0, 0.0, 0, 0.0, NULL)
+    assert r == _native.EINVAL
+
+
+def test_gated_and_norm_reject_bad_shapes():
+    lib = _native.lib()
+    assert lib.tileops_gelu_and_mul_fwd(NULL, NULL, -1, 8, 2, NULL) == _native.EBADSHAPE
+    assert lib.tileops_gelu_tanh_and_mul_fwd(NULL, NULL, 4, -8, 2, NULL) == _native.EBADSHAPE
+    assert lib.tileops_fused_add_layer_norm_fwd(
+        NULL, NULL, NULL, NULL, NULL, NULL, 4, 0, 1e-5, 2, 2, NULL) == _native.EBADSHAPE
+    assert lib.tileops_fused_add_layer_norm_fwd(
+        NULL, NULL, NULL, NULL, NULL, NULL, 4, 8, 1e-5, 2, 2, NULL) == _native.EINVAL
+
+
+def test_conv_rejects_bad_geometry():
+    lib = _native.lib()
+    args = [NULL] * 4
+    # k = 0
+    assert lib.tileops_conv1d_depthwise_fwd(*args, 1, 4, 16, 16, 0, 1, 0, 1, 2, 2, 0,
+                                            NULL) == _native.EBADSHAPE
+    # unknown activation
+    assert lib.tileops_conv1d_depthwise_fwd(*args, 1, 4, 16, 16, 3, 1, 1, 1, 2, 2, 7,
+                                            NULL) == _native.EINVAL
+    # c_in not divisible by groups
+    assert lib.tileops_conv1d_direct_fwd(*args, 1, 6, 16, 8, 16, 3, 1, 1, 1, 4, 1,
+                                         NULL) == _native.EBADSHAPE
+
+
+def test_status_maps_to_python_exceptions():
+    with pytest.raises(ValueError, match="invalid shape"):
+        _native.call("tileops_hardswish_fwd", NULL, NULL, -5, 0, NULL)
+    with pytest.raises(_native.NativeLibraryError):
+        _native.call("tileops_no_such_entry")

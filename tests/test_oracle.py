@@ -1,0 +1,125 @@
+"""Pin the CPU oracle to the reference: oracle(fixture inputs) == fixture outputs.
+
+The fixtures under tests/golden were computed by the reference's own ref
+programs and golden functions (tests/golden/make_golden.py).  The oracle is
+a restatement, so it must reproduce them bit for bit (NaN positions equal).
+CPU only.
+"""
+
+import pytest
+import torch
+
+from oracle import reference as ref
+from tests.golden.load import load, names
+
+
+def assert_same(out: torch.Tensor, expect: torch.Tensor) -> None:
+    assert out.dtype == expect.dtype and out.shape == expect.shape
+    if out.dtype.is_floating_point:
+        torch.testing.assert_close(out, expect, atol=0, rtol=0, equal_nan=True)
+    else:
+        assert torch.equal(out, expect)
+
+
+@pytest.mark.parametrize("name", names("hardswish_") + names("hardsigmoid_"))
+def test_oracle_unary(name):
+    case = load(name)
+    fn = ref.hardswish if name.startswith("hardswish") else ref.hardsigmoid
+    assert_same(fn(case["inputs"]["x"]), case["outputs"]["y"])
+
+
+@pytest.mark.parametrize("name", names("clamp_scalar_"))
+def test_oracle_clamp_scalar(name):
+    case = load(name)
+    m = case["meta"]
+    assert_same(ref.clamp_scalar(case["inputs"]["x"], m["min"], m["max"]), case["outputs"]["y"])
+
+
+@pytest.mark.parametrize("name", names("clamp_min_"))
+def test_oracle_clamp_min(name):
+    case = load(name)
+    assert_same(ref.clamp_min(case["inputs"]["x"], case["meta"]["min"]), case["outputs"]["y"])
+
+
+@pytest.mark.parametrize("name", names("isnan_") + names("isinf_") + names("isfinite_"))
+def test_oracle_predicates(name):
+    case = load(name)
+    fn = {"isnan": ref.isnan, "isinf": ref.isinf, "isfinite": ref.isfinite}[name.split("_")[0]]
+    assert_same(fn(case["inputs"]["x"]), case["outputs"]["y"])
+
+
+@pytest.mark.parametrize("name", names("bitwise_not_"))
+def test_oracle_bitwise_not(name):
+    case = load(name)
+    assert_same(ref.bitwise_not(case["inputs"]["x"]), case["outputs"]["y"])
+
+
+@pytest.mark.parametrize("name", names("gelu_and_mul_") + names("gelu_tanh_and_mul_"))
+def test_oracle_gated(name):
+    case = load(name)
+    x = case["inputs"]["x"]
+    if name.startswith("gelu_tanh"):
+        assert_same(ref.gelu_tanh_and_mul(x), case["outputs"]["y"])
+    elif "golden" in name:
+        # golden_gelu_and_mul uses F.gelu (exact erf form); the oracle writes
+        # the erf formula out, as the reference test does: equal within fp32 rounding.
+        torch.testing.assert_close(ref.gelu_and_mul(x), case["outputs"]["y"], atol=1e-6,
+                                   rtol=1e-6)
+    else:
+        assert_same(ref.gelu_and_mul(x), case["outputs"]["y"])
+
+
+@pytest.mark.parametrize("name", names("fused_add_layer_norm_"))
+def test_oracle_fused_add_layer_norm(name):
+    case = load(name)
+    i = case["inputs"]
+    y, added = ref.fused_add_layer_norm(i["x"], i["residual"], i["weight"], i["bias"],
+                                        case["meta"]["eps"])
+    assert_same(y, case["outputs"]["y"])
+    assert_same(added, case["outputs"]["residual_out"])
+
+
+@pytest.mark.parametrize("name", [n for n in names("conv1d_") if "golden" not in n])
+def test_oracle_conv1d(name):
+    case = load(name)
+    m, i = case["meta"], case["inputs"]
+    y = ref.conv1d(i["x"], i["weight"], i["bias"], stride=m["stride"], padding=m["padding"],
+                   dilation=m["dilation"], groups=m["groups"])
+    assert_same(y, case["outputs"]["y"])
+
+
+def test_oracle_causal_conv_matches_reference_depthwise_golden():
+    case = load("conv1d_depthwise_golden_causal_bf16")
+    i = case["inputs"]
+    length = i["x"].shape[-1]
+    y = ref.causal_depthwise_conv1d(i["x"], i["weight"], i["bias"])
+    assert_same(y, case["outputs"]["y_full"][..., :length].contiguous())
+
+
+@pytest.mark.parametrize("name", names("mha_"))
+def test_oracle_mha(name):
+    case = load(name)
+    i, m = case["inputs"], case["meta"]
+    o, lse = ref.gqa_prefill_fwd(i["q"], i["k"], i["v"], m["is_causal"])
+    assert_same(o, case["outputs"]["o_golden"])
+    assert_same(lse, case["outputs"]["lse"])
+    assert_same(ref.mha_sdpa(i["q"], i["k"], i["v"], m["is_causal"]), case["outputs"]["o_sdpa"])
+
+
+@pytest.mark.parametrize("name", names("gdn_"))
+def test_oracle_gdn(name):
+    case = load(name)
+    i, m = case["inputs"], case["meta"]
+    o, s = ref.gdn_sequential(i["q"], i["k"], i["v"], i["g"], i["beta"], i["state0"], m["scale"])
+    torch.testing.assert_close(o, case["outputs"]["o"], atol=1e-6, rtol=1e-6)
+    torch.testing.assert_close(s, case["outputs"]["final_state"], atol=1e-6, rtol=1e-6)
+
+
+def test_oracle_gdn_bthd_layout_matches_bhtd():
+    case = load("gdn_b1_h2_t48_d16_dv16")
+    i, m = case["inputs"], case["meta"]
+    t = lambda a: a.transpose(1, 2).contiguous()  # noqa: E731
+    o, s = ref.gdn_prefill_bthd(t(i["q"]), t(i["k"]), t(i["v"]), t(i["g"]), t(i["beta"]),
+                                m["scale"], i["state0"])
+    torch.testing.assert_close(o.float(), t(case["outputs"]["o"]).to(o.dtype).float())
+    torch.testing.assert_close(s, case["outputs"]["final_state"], atol=1e-6, rtol=1e-6)

@@ -1,0 +1,111 @@
+// Shared helpers for the sm_100a TileOPs kernels: dtype traits, 16-byte
+// vector access, launch geometry and argument checking for the C ABI.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/tileops_c.h"
+
+namespace tileops {
+
+// B200: 148 SMs.  Grids of streaming kernels are sized as a multiple of the
+// SM count (queried once per device, with 148 as the default).
+int sm_count();
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Map a launch error onto the ABI status.
+inline int launch_status() {
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? TILEOPS_OK : TILEOPS_ELAUNCH;
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+inline int dtype_size(int dt) {
+  switch (dt) {
+    case TILEOPS_DT_F32: return 4;
+    case TILEOPS_DT_F16: return 2;
+    case TILEOPS_DT_BF16: return 2;
+    case TILEOPS_DT_BOOL: return 1;
+    case TILEOPS_DT_U8: return 1;
+    case TILEOPS_DT_I8: return 1;
+    case TILEOPS_DT_I16: return 2;
+    case TILEOPS_DT_I32: return 4;
+    case TILEOPS_DT_I64: return 8;
+    default: return 0;
+  }
+}
+
+inline bool is_float_dtype(int dt) {
+  return dt == TILEOPS_DT_F32 || dt == TILEOPS_DT_F16 || dt == TILEOPS_DT_BF16;
+}
+
+// ---- scalar conversion (fp32 opmath, round-to-nearest-even on store) ----
+template <typename T>
+struct Cvt;
+template <>
+struct Cvt<float> {
+  static __device__ __forceinline__ float to_f(float v) { return v; }
+  static __device__ __forceinline__ float from_f(float v) { return v; }
+};
+template <>
+struct Cvt<__half> {
+  static __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
+  static __device__ __forceinline__ __half from_f(float v) { return __float2half_rn(v); }
+};
+template <>
+struct Cvt<__nv_bfloat16> {
+  static __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+  static __device__ __forceinline__ __nv_bfloat16 from_f(float v) {
+    return __float2bfloat16_rn(v);
+  }
+};
+
+// ---- 16-byte vectors ----
+// Streaming loads bypass L1 allocation (each byte is touched once); stores
+// use the evict-first (.cs) hint so the output stream does not displace
+// inputs still needed by other CTAs from L2.
+__device__ __forceinline__ uint4 ld_stream(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+__device__ __forceinline__ void st_stream(void* p, uint4 v) {
+  asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ uint2 ld_stream8(const void* p) {
+  uint2 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];"
+               : "=r"(r.x), "=r"(r.y)
+               : "l"(p));
+  return r;
+}
+__device__ __forceinline__ void st_stream8(void* p, uint2 v) {
+  asm volatile("st.global.cs.v2.u32 [%0], {%1,%2};" ::"l"(p), "r"(v.x), "r"(v.y) : "memory");
+}
+
+// Elements of T in one 16-byte vector, and a union for lane access.
+template <typename T>
+union Pack16 {
+  uint4 u;
+  T e[16 / sizeof(T)];
+};
+
+// Grid for a grid-stride streaming loop: enough CTAs to cover `work` items
+// of `per_cta` each, capped at `waves` full waves over the SMs.
+inline unsigned stream_grid(int64_t work, int64_t per_cta, int waves) {
+  int64_t need = (work + per_cta - 1) / per_cta;
+  int64_t cap = static_cast<int64_t>(sm_count()) * waves;
+  if (need < 1) need = 1;
+  return static_cast<unsigned>(need < cap ? need : cap);
+}
+
+}  // namespace tileops

@@ -1,0 +1,343 @@
+// Elementwise unary forward kernels: hardswish, hardsigmoid, clamp (float in,
+// same dtype out), isnan / isinf / isfinite (float in, bool out) and
+// bitwise_not (integer / bool byte stream).
+//
+// All of them are HBM-streaming: one read and one write per element.  The
+// vector path moves 16-byte packets with L1-bypassing loads and evict-first
+// stores, UNROLL packets in flight per thread, over a grid-stride loop sized
+// to a few waves of the 148 SMs.  Ragged tails (n not a multiple of the
+// packet) are finished by block 0; misaligned pointers take a scalar kernel.
+//
+// Reference semantics (examples/TileOPs in Yihuace/tile-ascendnpu-ops):
+//   hardswish   ops/elementwise/hardswish.py:27-107, test ref F.hardswish(x.float())
+//   hardsigmoid ops/elementwise/hardsigmoid.py:27-107, NaN propagates
+//   clamp       ops/elementwise/clamp_scalar.py:30-111, torch.clamp(x.float(), min, max)
+//   is*         ops/elementwise/{isnan,isinf,isfinite}.py, exact bool output
+//   bitwise_not ops/elementwise/bitwise_not.py:33-119, bool is logical not
+#include "common.cuh"
+
+namespace tileops {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kUnroll = 4;
+
+// ---------------------------------------------------------------- functors
+struct HardswishF {
+  __device__ __forceinline__ float operator()(float x) const {
+    // x * min(max(x + 3, 0), 6) / 6, evaluated left to right like torch.
+    const float t = fminf(fmaxf(x + 3.0f, 0.0f), 6.0f);
+    return x * t / 6.0f;
+  }
+};
+
+struct HardsigmoidF {
+  __device__ __forceinline__ float operator()(float x) const {
+    if (x != x) return x;  // NaN in -> NaN out (torch's maximum/minimum propagate it)
+    return fminf(fmaxf(x + 3.0f, 0.0f), 6.0f) / 6.0f;
+  }
+};
+
+struct ClampF {
+  float lo, hi;
+  int has_lo, has_hi;
+  __device__ __forceinline__ float operator()(float x) const {
+    float r = x;
+    // NaN in either operand propagates, as torch.clamp does.
+    if (has_lo) r = (r != r) ? r : ((lo != lo) ? lo : fmaxf(r, lo));
+    if (has_hi) r = (r != r) ? r : ((hi != hi) ? hi : fminf(r, hi));
+    return r;
+  }
+};
+
+// ------------------------------------------------------ float -> float map
+template <typename T, typename F>
+__global__ void __launch_bounds__(kThreads)
+    unary_map_vec(const T* __restrict__ x, T* __restrict__ y, int64_t n, F f) {
+  constexpr int V = 16 / sizeof(T);
+  const int64_t nvec = n / V;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
+  int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+  for (; i + (kUnroll - 1) * stride < nvec; i += kUnroll * stride) {
+    Pack16<T> p[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) p[u].u = ld_stream(x + (i + u * stride) * V);
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+#pragma unroll
+      for (int e = 0; e < V; ++e) p[u].e[e] = Cvt<T>::from_f(f(Cvt<T>::to_f(p[u].e[e])));
+      st_stream(y + (i + u * stride) * V, p[u].u);
+    }
+  }
+  for (; i < nvec; i += stride) {
+    Pack16<T> p;
+    p.u = ld_stream(x + i * V);
+#pragma unroll
+    for (int e = 0; e < V; ++e) p.e[e] = Cvt<T>::from_f(f(Cvt<T>::to_f(p.e[e])));
+    st_stream(y + i * V, p.u);
+  }
+  if (blockIdx.x == 0 && threadIdx.x < n - nvec * V) {
+    const int64_t j = nvec * V + threadIdx.x;
+    y[j] = Cvt<T>::from_f(f(Cvt<T>::to_f(x[j])));
+  }
+}
+
+template <typename T, typename F>
+__global__ void __launch_bounds__(kThreads)
+    unary_map_scalar(const T* __restrict__ x, T* __restrict__ y, int64_t n, F f) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < n; i += stride)
+    y[i] = Cvt<T>::from_f(f(Cvt<T>::to_f(x[i])));
+}
+
+template <typename T, typename F>
+int launch_map_t(const void* x, void* y, int64_t n, F f, cudaStream_t s) {
+  const T* xp = static_cast<const T*>(x);
+  T* yp = static_cast<T*>(y);
+  if (aligned16(x) && aligned16(y)) {
+    constexpr int V = 16 / sizeof(T);
+    const unsigned grid = stream_grid(n / V + 1, static_cast<int64_t>(kThreads) * kUnroll, 8);
+    unary_map_vec<T, F><<<grid, kThreads, 0, s>>>(xp, yp, n, f);
+  } else {
+    const unsigned grid = stream_grid(n, kThreads, 8);
+    unary_map_scalar<T, F><<<grid, kThreads, 0, s>>>(xp, yp, n, f);
+  }
+  return launch_status();
+}
+
+template <typename F>
+int launch_map(const void* x, void* y, int64_t n, int dtype, F f, void* stream) {
+  if (n < 0) return TILEOPS_EBADSHAPE;
+  if (n == 0) return TILEOPS_OK;
+  if (!x || !y) return TILEOPS_EINVAL;
+  cudaStream_t s = as_stream(stream);
+  switch (dtype) {
+    case TILEOPS_DT_F32: return launch_map_t<float>(x, y, n, f, s);
+    case TILEOPS_DT_F16: return launch_map_t<__half>(x, y, n, f, s);
+    case TILEOPS_DT_BF16: return launch_map_t<__nv_bfloat16>(x, y, n, f, s);
+    default: return TILEOPS_EBADDTYPE;
+  }
+}
+
+// ------------------------------------------------------- float predicates
+// Bit tests on the raw encoding: the exponent field all-ones marks Inf/NaN,
+// and a non-zero mantissa under it marks NaN.  Exact for every input.
+enum class Pred { kNan, kInf, kFinite };
+
+template <typename T>
+struct Bits;
+template <>
+struct Bits<float> {
+  using U = uint32_t;
+  static constexpr U kAbs = 0x7fffffffu, kExp = 0x7f800000u;
+};
+template <>
+struct Bits<__half> {
+  using U = uint16_t;
+  static constexpr U kAbs = 0x7fff, kExp = 0x7c00;
+};
+template <>
+struct Bits<__nv_bfloat16> {
+  using U = uint16_t;
+  static constexpr U kAbs = 0x7fff, kExp = 0x7f80;
+};
+
+template <typename T, Pred P>
+__device__ __forceinline__ uint8_t pred_bits(typename Bits<T>::U u) {
+  using B = Bits<T>;
+  const typename Bits<T>::U a = u & B::kAbs;
+  if (P == Pred::kNan) return a > B::kExp;
+  if (P == Pred::kInf) return a == B::kExp;
+  return (u & B::kExp) != B::kExp;
+}
+
+// 16 elements per packet: 16*sizeof(T) bytes in, one 16-byte bool packet out.
+template <typename T, Pred P>
+__global__ void __launch_bounds__(kThreads)
+    predicate_vec(const T* __restrict__ x, uint8_t* __restrict__ y, int64_t n) {
+  using U = typename Bits<T>::U;
+  constexpr int kIn = sizeof(T);  // 16-byte loads per packet
+  const int64_t npk = n / 16;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
+  int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+  for (; i + stride < npk; i += 2 * stride) {
+    union {
+      uint4 u[kIn];
+      U b[16];
+    } in[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r)
+#pragma unroll
+      for (int q = 0; q < kIn; ++q)
+        in[r].u[q] = ld_stream(reinterpret_cast<const uint8_t*>(x) + (i + r * stride) * 16 * kIn + q * 16);
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      Pack16<uint8_t> o;
+#pragma unroll
+      for (int e = 0; e < 16; ++e) o.e[e] = pred_bits<T, P>(in[r].b[e]);
+      st_stream(y + (i + r * stride) * 16, o.u);
+    }
+  }
+  for (; i < npk; i += stride) {
+    union {
+      uint4 u[kIn];
+      U b[16];
+    } in;
+#pragma unroll
+    for (int q = 0; q < kIn; ++q)
+      in.u[q] = ld_stream(reinterpret_cast<const uint8_t*>(x) + i * 16 * kIn + q * 16);
+    Pack16<uint8_t> o;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) o.e[e] = pred_bits<T, P>(in.b[e]);
+    st_stream(y + i * 16, o.u);
+  }
+  if (blockIdx.x == 0 && threadIdx.x < n - npk * 16) {
+    const int64_t j = npk * 16 + threadIdx.x;
+    y[j] = pred_bits<T, P>(reinterpret_cast<const U*>(x)[j]);
+  }
+}
+
+template <typename T, Pred P>
+__global__ void __launch_bounds__(kThreads)
+    predicate_scalar(const T* __restrict__ x, uint8_t* __restrict__ y, int64_t n) {
+  using U = typename Bits<T>::U;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < n; i += stride)
+    y[i] = pred_bits<T, P>(reinterpret_cast<const U*>(x)[i]);
+}
+
+template <typename T, Pred P>
+int launch_pred_t(const void* x, void* y, int64_t n, cudaStream_t s) {
+  const T* xp = static_cast<const T*>(x);
+  uint8_t* yp = static_cast<uint8_t*>(y);
+  if (aligned16(x) && aligned16(y)) {
+    const unsigned grid = stream_grid(n / 16 + 1, kThreads * 2, 8);
+    predicate_vec<T, P><<<grid, kThreads, 0, s>>>(xp, yp, n);
+  } else {
+    predicate_scalar<T, P><<<stream_grid(n, kThreads, 8), kThreads, 0, s>>>(xp, yp, n);
+  }
+  return launch_status();
+}
+
+template <Pred P>
+int launch_pred(const void* x, void* y, int64_t n, int dtype, void* stream) {
+  if (n < 0) return TILEOPS_EBADSHAPE;
+  if (n == 0) return TILEOPS_OK;
+  if (!x || !y) return TILEOPS_EINVAL;
+  cudaStream_t s = as_stream(stream);
+  switch (dtype) {
+    case TILEOPS_DT_F32: return launch_pred_t<float, P>(x, y, n, s);
+    case TILEOPS_DT_F16: return launch_pred_t<__half, P>(x, y, n, s);
+    case TILEOPS_DT_BF16: return launch_pred_t<__nv_bfloat16, P>(x, y, n, s);
+    default: return TILEOPS_EBADDTYPE;
+  }
+}
+
+// ------------------------------------------------------------ bitwise not
+// ~x is a byte-wise complement for every integer width; torch.bool stores
+// 0/1 bytes, so logical not is x ^ 1 per byte.  Both run as one XOR stream.
+__global__ void __launch_bounds__(kThreads)
+    xor_stream_vec(const uint8_t* __restrict__ x, uint8_t* __restrict__ y, int64_t nbytes,
+                   uint32_t mask) {
+  const int64_t nvec = nbytes / 16;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
+  int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+  for (; i + (kUnroll - 1) * stride < nvec; i += kUnroll * stride) {
+    uint4 p[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) p[u] = ld_stream(x + (i + u * stride) * 16);
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      p[u].x ^= mask;
+      p[u].y ^= mask;
+      p[u].z ^= mask;
+      p[u].w ^= mask;
+      st_stream(y + (i + u * stride) * 16, p[u]);
+    }
+  }
+  for (; i < nvec; i += stride) {
+    uint4 p = ld_stream(x + i * 16);
+    p.x ^= mask;
+    p.y ^= mask;
+    p.z ^= mask;
+    p.w ^= mask;
+    st_stream(y + i * 16, p);
+  }
+  if (blockIdx.x == 0 && threadIdx.x < nbytes - nvec * 16) {
+    const int64_t j = nvec * 16 + threadIdx.x;
+    y[j] = x[j] ^ static_cast<uint8_t>(mask & 0xffu);
+  }
+}
+
+__global__ void __launch_bounds__(kThreads)
+    xor_stream_scalar(const uint8_t* __restrict__ x, uint8_t* __restrict__ y, int64_t nbytes,
+                      uint8_t mask) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < nbytes;
+       i += stride)
+    y[i] = x[i] ^ mask;
+}
+
+}  // namespace
+}  // namespace tileops
+
+using namespace tileops;
+
+extern "C" int tileops_hardswish_fwd(const void* x, void* y, int64_t n, int dtype,
+                                     void* stream) {
+  return launch_map(x, y, n, dtype, HardswishF{}, stream);
+}
+
+extern "C" int tileops_hardsigmoid_fwd(const void* x, void* y, int64_t n, int dtype,
+                                       void* stream) {
+  return launch_map(x, y, n, dtype, HardsigmoidF{}, stream);
+}
+
+extern "C" int tileops_clamp_scalar_fwd(const void* x, void* y, int64_t n, int dtype,
+                                        int has_min, double min_val, int has_max,
+                                        double max_val, void* stream) {
+  if (!has_min && !has_max) return TILEOPS_EINVAL;
+  ClampF f{static_cast<float>(min_val), static_cast<float>(max_val), has_min ? 1 : 0,
+           has_max ? 1 : 0};
+  return launch_map(x, y, n, dtype, f, stream);
+}
+
+extern "C" int tileops_isnan_fwd(const void* x, void* y, int64_t n, int dtype, void* stream) {
+  return launch_pred<Pred::kNan>(x, y, n, dtype, stream);
+}
+extern "C" int tileops_isinf_fwd(const void* x, void* y, int64_t n, int dtype, void* stream) {
+  return launch_pred<Pred::kInf>(x, y, n, dtype, stream);
+}
+extern "C" int tileops_isfinite_fwd(const void* x, void* y, int64_t n, int dtype,
+                                    void* stream) {
+  return launch_pred<Pred::kFinite>(x, y, n, dtype, stream);
+}
+
+extern "C" int tileops_bitwise_not_fwd(const void* x, void* y, int64_t n, int dtype,
+                                       void* stream) {
+  if (n < 0) return TILEOPS_EBADSHAPE;
+  uint32_t mask;
+  switch (dtype) {
+    case TILEOPS_DT_BOOL: mask = 0x01010101u; break;
+    case TILEOPS_DT_U8:
+    case TILEOPS_DT_I8:
+    case TILEOPS_DT_I16:
+    case TILEOPS_DT_I32:
+    case TILEOPS_DT_I64: mask = 0xffffffffu; break;
+    default: return TILEOPS_EBADDTYPE;
+  }
+  if (n == 0) return TILEOPS_OK;
+  if (!x || !y) return TILEOPS_EINVAL;
+  const int64_t nbytes = n * dtype_size(dtype);
+  cudaStream_t s = as_stream(stream);
+  const uint8_t* xp = static_cast<const uint8_t*>(x);
+  uint8_t* yp = static_cast<uint8_t*>(y);
+  if (aligned16(x) && aligned16(y)) {
+    const unsigned grid = stream_grid(nbytes / 16 + 1, kThreads * kUnroll, 8);
+    xor_stream_vec<<<grid, kThreads, 0, s>>>(xp, yp, nbytes, mask);
+  } else {
+    xor_stream_scalar<<<stream_grid(nbytes, kThreads, 8), kThreads, 0, s>>>(
+        xp, yp, nbytes, static_cast<uint8_t>(mask & 0xffu));
+  }
+  return launch_status();
+}

@@ -1,0 +1,138 @@
+// Gated activations: y[r, c] = act(x[r, c]) * x[r, N + c] for x of shape
+// (M, 2N), y of shape (M, N).  act is the exact erf GELU or the tanh GELU.
+//
+// HBM-bound (3 * M * N * elem bytes per call).  The vector path gives each
+// thread a 16-byte packet of the gate half and the matching packet of the
+// value half (both coalesced across the warp, since packets of one warp are
+// consecutive columns of one row), computes in fp32 and rounds once.  Two
+// packet pairs are kept in flight per thread.  Rows whose width N is not a
+// multiple of the packet, or misaligned pointers, take the scalar kernel.
+//
+// Reference: ops/elementwise/gelu_and_mul.py:42-125 and the test
+// ref_program tests/ops/test_gelu_and_mul.py:63-76 (explicit erf, fp32);
+// ops/elementwise/gelu_tanh_and_mul.py:43-126 with
+// tests/ops/test_gelu_tanh_and_mul.py:64-86 (explicit tanh formula).
+#include "common.cuh"
+
+namespace tileops {
+namespace {
+
+constexpr int kThreads = 256;
+
+struct GeluErfF {
+  __device__ __forceinline__ float operator()(float g, float v) const {
+    // 0.5 * g * (1 + erf(g * sqrt(0.5))) * v, same association as the reference.
+    const float gelu = 0.5f * g * (1.0f + erff(g * 0.70710678118654752f));
+    return gelu * v;
+  }
+};
+
+struct GeluTanhF {
+  __device__ __forceinline__ float operator()(float g, float v) const {
+    // sqrt(2/pi) * (g + 0.044715 g^3), then 0.5 g (1 + tanh(inner)).
+    const float inner = 0.79788456080286536f * (g + 0.044715f * (g * g * g));
+    const float gelu = 0.5f * g * (1.0f + tanhf(inner));
+    return gelu * v;
+  }
+};
+
+template <typename T, typename F>
+__global__ void __launch_bounds__(kThreads)
+    gated_vec(const T* __restrict__ x, T* __restrict__ y, int64_t M, int64_t N, F f) {
+  constexpr int V = 16 / sizeof(T);
+  const int64_t pk_per_row = N / V;
+  const int64_t total = M * pk_per_row;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
+  int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+  for (; i + stride < total; i += 2 * stride) {
+    Pack16<T> g[2], v[2];
+    int64_t out_off[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int64_t p = i + u * stride;
+      const int64_t r = p / pk_per_row;
+      const int64_t c = (p - r * pk_per_row) * V;
+      const T* row = x + r * 2 * N;
+      g[u].u = ld_stream(row + c);
+      v[u].u = ld_stream(row + N + c);
+      out_off[u] = r * N + c;
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      Pack16<T> o;
+#pragma unroll
+      for (int e = 0; e < V; ++e)
+        o.e[e] = Cvt<T>::from_f(f(Cvt<T>::to_f(g[u].e[e]), Cvt<T>::to_f(v[u].e[e])));
+      st_stream(y + out_off[u], o.u);
+    }
+  }
+  for (; i < total; i += stride) {
+    const int64_t r = i / pk_per_row;
+    const int64_t c = (i - r * pk_per_row) * V;
+    const T* row = x + r * 2 * N;
+    Pack16<T> g, v, o;
+    g.u = ld_stream(row + c);
+    v.u = ld_stream(row + N + c);
+#pragma unroll
+    for (int e = 0; e < V; ++e)
+      o.e[e] = Cvt<T>::from_f(f(Cvt<T>::to_f(g.e[e]), Cvt<T>::to_f(v.e[e])));
+    st_stream(y + r * N + c, o.u);
+  }
+}
+
+template <typename T, typename F>
+__global__ void __launch_bounds__(kThreads)
+    gated_scalar(const T* __restrict__ x, T* __restrict__ y, int64_t M, int64_t N, F f) {
+  const int64_t total = M * N;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; i < total;
+       i += stride) {
+    const int64_t r = i / N;
+    const int64_t c = i - r * N;
+    const T* row = x + r * 2 * N;
+    y[i] = Cvt<T>::from_f(f(Cvt<T>::to_f(row[c]), Cvt<T>::to_f(row[N + c])));
+  }
+}
+
+template <typename T, typename F>
+int launch_gated_t(const void* x, void* y, int64_t M, int64_t N, F f, cudaStream_t s) {
+  constexpr int V = 16 / sizeof(T);
+  const T* xp = static_cast<const T*>(x);
+  T* yp = static_cast<T*>(y);
+  if (N % V == 0 && aligned16(x) && aligned16(y)) {
+    const int64_t total = M * (N / V);
+    gated_vec<T, F><<<stream_grid(total, kThreads * 2, 8), kThreads, 0, s>>>(xp, yp, M, N, f);
+  } else {
+    gated_scalar<T, F><<<stream_grid(M * N, kThreads, 8), kThreads, 0, s>>>(xp, yp, M, N, f);
+  }
+  return launch_status();
+}
+
+template <typename F>
+int launch_gated(const void* x, void* y, int64_t M, int64_t N, int dtype, F f, void* stream) {
+  if (M < 0 || N < 0) return TILEOPS_EBADSHAPE;
+  if (M == 0 || N == 0) return TILEOPS_OK;
+  if (!x || !y) return TILEOPS_EINVAL;
+  cudaStream_t s = as_stream(stream);
+  switch (dtype) {
+    case TILEOPS_DT_F32: return launch_gated_t<float>(x, y, M, N, f, s);
+    case TILEOPS_DT_F16: return launch_gated_t<__half>(x, y, M, N, f, s);
+    case TILEOPS_DT_BF16: return launch_gated_t<__nv_bfloat16>(x, y, M, N, f, s);
+    default: return TILEOPS_EBADDTYPE;
+  }
+}
+
+}  // namespace
+}  // namespace tileops
+
+using namespace tileops;
+
+extern "C" int tileops_gelu_and_mul_fwd(const void* x, void* y, int64_t M, int64_t N, int dtype,
+                                        void* stream) {
+  return launch_gated(x, y, M, N, dtype, GeluErfF{}, stream);
+}
+
+extern "C" int tileops_gelu_tanh_and_mul_fwd(const void* x, void* y, int64_t M, int64_t N,
+                                             int dtype, void* stream) {
+  return launch_gated(x, y, M, N, dtype, GeluTanhF{}, stream);
+}
