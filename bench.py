@@ -212,6 +212,42 @@ def _causal_conv(activation) -> Workload:
     )
 
 
+def _mha(causal: bool) -> Workload:
+    from tileops.ops.attention import MultiHeadAttentionFwdOp
+
+    B, S, H, D = 8, 4096, 32, 128
+
+    def make(dev, seed):
+        g = torch.Generator(device="cpu").manual_seed(seed)
+        return tuple(torch.randn(B, S, H, D, generator=g).to(torch.bfloat16).to(dev)
+                     for _ in range(3))
+
+    def cpu(inp):
+        from oracle import reference as ref
+
+        return ref.gqa_prefill_fwd(*inp, causal)
+
+    def sample(inp, rows):
+        s = max(128, min(S, rows * 4))
+        return tuple(t[:1, :s, :1].contiguous() for t in inp)
+
+    def units(inp):
+        s = inp[0].shape[1]
+        f = 4.0 * s * s * D
+        return f / 2 if causal else f
+
+    return Workload(
+        name="mha_causal" if causal else "mha", unit="TFLOP/s", dtype="bf16", bound="tensor",
+        metric="achieved TFLOP/s (MultiHeadAttentionFwdOp)",
+        config={"workload": f"MultiHeadAttentionFwdOp q/k/v (8, 4096, 32, 128) bf16 BSHD, "
+                            f"causal={causal}, scale 1/sqrt(128) (BASELINE configs[3])"},
+        make_inputs=make,
+        build_op=lambda: MultiHeadAttentionFwdOp(B, H, S, D, causal, torch.bfloat16),
+        run=lambda op, inp: op(*inp), work_per_step=lambda op: float(op.eval_roofline()[0]),
+        kernel_regex="attn_fwd_kernel", cpu_fn=cpu, cpu_slice=sample, cpu_units=units,
+    )
+
+
 def workloads() -> dict[str, Callable[[], Workload]]:
     table = {
         "fused_add_layer_norm": _faln,
@@ -219,6 +255,8 @@ def workloads() -> dict[str, Callable[[], Workload]]:
         "gelu_tanh_and_mul": lambda: _gated(True),
         "causal_conv1d": lambda: _causal_conv(None),
         "causal_conv1d_silu": lambda: _causal_conv("silu"),
+        "mha": lambda: _mha(False),
+        "mha_causal": lambda: _mha(True),
     }
     for kind in ("hardswish", "hardsigmoid", "clamp_scalar", "isnan", "isinf", "isfinite",
                  "bitwise_not"):

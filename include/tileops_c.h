@@ -148,6 +148,22 @@ int tileops_conv1d_direct_fwd(const void* x, const void* w, const void* bias, vo
                               int64_t l_out, int64_t k, int64_t stride, int64_t pad_left,
                               int64_t dilation, int64_t groups, int dtype, void* stream);
 
+/* ---- attention ----------------------------------------------------------- */
+
+/* Flash-style multi-head / grouped-query attention forward on tcgen05 tensor
+ * cores, BSHD layout.  q (B, Sq, H, D), k / v (B, Skv, Hkv, D) of dtype
+ * f16/bf16 (D = 64 or 128, H % Hkv == 0), o like q, lse (B, H, Sq) fp32 in the
+ * log2 domain: lse = logsumexp(scale * q k^T) / ln 2.  Causal masking is
+ * right-aligned (query i sees keys j <= i + Skv - Sq; needs Sq <= Skv).
+ * q, k, v, o must be 16-byte aligned (TMA).  A bounded device-side wait that
+ * times out is reported through tileops_device_error_flag.
+ * Replaces _gqa_prefill_fwd_kernel,
+ * kernels/attention/multi_head_attention/multi_head_attention_kernel/perf_opt/_gqa_prefill_fwd_kernel.py:199. */
+int tileops_mha_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
+                    int64_t batch, int64_t heads, int64_t heads_kv, int64_t seq_q,
+                    int64_t seq_kv, int64_t dim, int is_causal, double sm_scale, int dtype,
+                    void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -81,3 +81,26 @@ def test_misaligned_input_view():
 def test_empty_rows():
     x = torch.empty(0, 16, device="cuda", dtype=torch.float16)
     assert GeluAndMulFwdOp(0, 8, torch.float16)(x).shape == (0, 8)
+
+
+@pytest.mark.parametrize("op_cls", [GeluAndMulFwdOp, GeluTanhAndMulFwdOp])
+def test_activation_accuracy_dense_grid(op_cls):
+    """The kernels evaluate erf by Abramowitz & Stegun 7.1.26 (|error| <= 1.5e-7)
+    and tanh as 1 - 2 / (1 + exp(2u)); against fp64 the GELU error must stay
+    below 0.5 * |g| * 3e-7 (approximation bound plus the approximate reciprocal
+    and exp2), i.e. 2e-6 on [-12, 12], and the IEEE limits must hold."""
+    g = torch.linspace(-12.0, 12.0, 200_001, dtype=torch.float64)
+    g = torch.cat([g, torch.tensor([0.0, -0.0, 1e-30, -1e-30, float("inf"), float("-inf"),
+                                    float("nan")], dtype=torch.float64)])
+    n = g.numel()
+    x = torch.cat([g.float(), torch.ones(n)]).reshape(1, 2 * n).cuda()  # gate | value = 1
+    y = op_cls(1, n, torch.float32)(x).cpu().double()[0]
+    g32 = g.float().double()
+    if op_cls is GeluAndMulFwdOp:
+        exact = 0.5 * g32 * (1.0 + torch.erf(g32 / 2**0.5))
+    else:
+        exact = 0.5 * g32 * (1.0 + torch.tanh((2 / torch.pi) ** 0.5 * (g32 + 0.044715 * g32**3)))
+    finite = torch.isfinite(g32)
+    err = (y[finite] - exact[finite]).abs()
+    assert float(err.max()) <= 2e-6, float(err.max())
+    assert y[-3] == float("inf") and torch.isnan(y[-2]) and torch.isnan(y[-1])

@@ -1,0 +1,155 @@
+"""GPU parity of MultiHeadAttentionFwdOp (tcgen05 / TMEM flash attention).
+
+Ported from TO/tests/ops/test_multi_head_attention.py: the (batch, seq_len,
+heads, dim, causal, dtype) sweep, output checked against SDPA with the
+reference tolerance atol 5e-3 / rtol 1e-5, the GQA-kernel dispatch and the
+roofline formula.  Added: the log2-domain LSE against the reference golden
+(golden_gqa_prefill_fwd, restated in the oracle), the reference-output
+fixtures, causal masks, GQA (heads_kv < heads), sequence lengths that are not
+multiples of the 128-row tile, run-to-run determinism, and BASELINE's
+(8, 4096, 32, 128) configuration checked on sampled (batch, head) pairs
+(heads are independent, so a sampled head is an exact check).
+"""
+
+import pytest
+import torch
+
+from oracle import reference as ref
+from tests.golden.load import load, names
+from tileops.kernels.attention.multi_head_attention import GQAPrefillFwdKernel
+from tileops.ops.attention import MultiHeadAttentionFwdOp
+from tileops.testing.test_base import TestBase
+from tileops.workloads.attention import MhaFwdWorkload
+
+pytestmark = pytest.mark.gpu
+
+LSE_TOL = dict(atol=2e-3, rtol=1e-4)
+
+
+def out_tol(dtype):
+    """Output tolerance for the cases this build adds (causal, ragged, GQA).
+
+    The reference's own cases keep its atol 5e-3 / rtol 1e-5; that bound is
+    below one bf16 ulp (2**-8 relative) for outputs of magnitude > 0.64,
+    which causal early rows and very short sequences produce (few keys
+    averaged), so added cases use the north-star tolerance for 16-bit
+    outputs: 1e-2 / 1e-2 (bf16), 5e-3 / 5e-3 (fp16).
+    """
+    return dict(atol=1e-2, rtol=1e-2) if dtype == torch.bfloat16 else dict(atol=5e-3, rtol=5e-3)
+
+
+class MhaFwdTest(MhaFwdWorkload, TestBase):
+    def ref_program(self, q, k, v):
+        return ref.mha_sdpa(q, k, v, self.is_causal), None  # lse unchecked, as in the reference
+
+
+PARAMS = [
+    pytest.param(1, 1024, 8, 64, False, torch.float16, marks=pytest.mark.smoke),
+    pytest.param(1, 1024, 8, 64, False, torch.bfloat16, marks=pytest.mark.smoke),
+    pytest.param(1, 1024, 8, 64, True, torch.bfloat16, marks=pytest.mark.smoke),
+    pytest.param(2, 512, 4, 128, True, torch.float16, marks=pytest.mark.smoke),
+    pytest.param(4, 2048, 4, 128, False, torch.float16, marks=pytest.mark.full),
+    pytest.param(2, 4096, 4, 128, False, torch.bfloat16, marks=pytest.mark.full),
+    pytest.param(2, 2048, 8, 128, True, torch.bfloat16, marks=pytest.mark.full),
+]
+
+
+@pytest.mark.parametrize("batch, seq_len, heads, dim, causal, dtype", PARAMS)
+def test_mha_fwd(batch, seq_len, heads, dim, causal, dtype):
+    test = MhaFwdTest(batch, heads, seq_len, dim, causal, dtype)
+    op = MultiHeadAttentionFwdOp(batch, heads, seq_len, dim, causal, dtype)
+    tol = out_tol(dtype) if causal else dict(atol=5e-3, rtol=1e-5)  # reference cases: non-causal
+    test.check(op, *test.gen_inputs(), **tol)
+
+
+@pytest.mark.parametrize("seq_len", [1, 7, 128, 129, 200, 1000])
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("dim", [64, 128])
+def test_mha_ragged_lengths_and_lse(seq_len, causal, dim):
+    q, k, v = MhaFwdWorkload(1, 2, seq_len, dim, causal, torch.bfloat16).gen_inputs()
+    o, lse = MultiHeadAttentionFwdOp(1, 2, seq_len, dim, causal, torch.bfloat16)(q, k, v)
+    o_ref, lse_ref = ref.gqa_prefill_fwd(q, k, v, causal)
+    torch.testing.assert_close(o.cpu(), ref.mha_sdpa(q, k, v, causal), **out_tol(q.dtype))
+    torch.testing.assert_close(o.cpu(), o_ref, **out_tol(q.dtype))
+    torch.testing.assert_close(lse.cpu(), lse_ref, **LSE_TOL)
+
+
+@pytest.mark.parametrize("heads, heads_kv", [(8, 2), (4, 1), (6, 3)])
+@pytest.mark.parametrize("causal", [False, True])
+def test_gqa(heads, heads_kv, causal):
+    b, s, d = 2, 384, 128
+    q = torch.randn(b, s, heads, d, device="cuda", dtype=torch.bfloat16)
+    k = torch.randn(b, s, heads_kv, d, device="cuda", dtype=torch.bfloat16)
+    v = torch.randn(b, s, heads_kv, d, device="cuda", dtype=torch.bfloat16)
+    kern = GQAPrefillFwdKernel(b, heads, heads_kv, s, s, d, causal, torch.bfloat16)
+    o, lse = kern(q, k, v)
+    o_ref, lse_ref = ref.gqa_prefill_fwd(q, k, v, causal)
+    torch.testing.assert_close(o.cpu(), o_ref, **out_tol(q.dtype))
+    torch.testing.assert_close(lse.cpu(), lse_ref, **LSE_TOL)
+
+
+@pytest.mark.parametrize("sq, skv", [(100, 300), (128, 512), (1, 257)])
+@pytest.mark.parametrize("causal", [False, True])
+def test_unequal_lengths_right_aligned_causal(sq, skv, causal):
+    q = torch.randn(1, sq, 2, 64, device="cuda", dtype=torch.float16)
+    k = torch.randn(1, skv, 2, 64, device="cuda", dtype=torch.float16)
+    v = torch.randn(1, skv, 2, 64, device="cuda", dtype=torch.float16)
+    o, lse = GQAPrefillFwdKernel(1, 2, 2, sq, skv, 64, causal, torch.float16)(q, k, v)
+    o_ref, lse_ref = ref.gqa_prefill_fwd(q, k, v, causal)
+    torch.testing.assert_close(o.cpu(), o_ref, **out_tol(q.dtype))
+    torch.testing.assert_close(lse.cpu(), lse_ref, **LSE_TOL)
+
+
+@pytest.mark.parametrize("name", names("mha_"))
+def test_reference_fixture(name):
+    case = load(name)
+    i, m = case["inputs"], case["meta"]
+    q, k, v = (i[n].cuda() for n in ("q", "k", "v"))
+    b, s, h, d = q.shape
+    o, lse = MultiHeadAttentionFwdOp(b, h, s, d, m["is_causal"], q.dtype)(q, k, v)
+    tol = out_tol(q.dtype) if m["is_causal"] else dict(atol=5e-3, rtol=1e-5)
+    torch.testing.assert_close(o.cpu(), case["outputs"]["o_sdpa"], **tol)
+    torch.testing.assert_close(o.cpu(), case["outputs"]["o_golden"], **tol)
+    torch.testing.assert_close(lse.cpu(), case["outputs"]["lse"], **LSE_TOL)
+
+
+def test_deterministic():
+    q, k, v = MhaFwdWorkload(2, 4, 512, 128, True, torch.bfloat16).gen_inputs()
+    op = MultiHeadAttentionFwdOp(2, 4, 512, 128, True, torch.bfloat16)
+    o0, l0 = op(q, k, v)
+    for _ in range(2):
+        o1, l1 = op(q, k, v)
+        assert torch.equal(o0, o1) and torch.equal(l0, l1)
+
+
+def test_no_device_error_flag():
+    from tileops import _native
+
+    q, k, v = MhaFwdWorkload(1, 2, 256, 128, False, torch.bfloat16).gen_inputs()
+    MultiHeadAttentionFwdOp(1, 2, 256, 128, False, torch.bfloat16)(q, k, v)
+    torch.cuda.synchronize()
+    stream = _native.stream_handle(q.device)
+    assert _native.lib().tileops_device_error_flag(stream, 1) == 0
+
+
+@pytest.mark.full
+@pytest.mark.parametrize("causal", [True, False])
+def test_baseline_config_sampled_heads(causal):
+    """BASELINE: q/k/v (8, 4096, 32, 128) bf16; two (b, h) pairs checked exactly."""
+    b, s, h, d = 8, 4096, 32, 128
+    q, k, v = MhaFwdWorkload(b, h, s, d, causal, torch.bfloat16).gen_inputs()
+    o, lse = MultiHeadAttentionFwdOp(b, h, s, d, causal, torch.bfloat16)(q, k, v)
+    for bi, hi in ((0, 0), (7, 31)):
+        sl = (slice(bi, bi + 1), slice(None), slice(hi, hi + 1))
+        o_ref, lse_ref = ref.gqa_prefill_fwd(q[sl], k[sl], v[sl], causal)
+        torch.testing.assert_close(o[sl].cpu(), o_ref, **out_tol(q.dtype))
+        torch.testing.assert_close(lse[bi : bi + 1, hi : hi + 1].cpu(), lse_ref, **LSE_TOL)
+
+
+def test_rejects_bad_shapes():
+    q = torch.randn(1, 64, 2, 64, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="q.shape"):
+        MultiHeadAttentionFwdOp(1, 2, 32, 64, False, torch.bfloat16)(q, q, q)
+    with pytest.raises(ValueError):  # head dim 96 has no kernel
+        MultiHeadAttentionFwdOp(1, 2, 64, 96, False, torch.bfloat16)(
+            *(torch.randn(1, 64, 2, 96, device="cuda", dtype=torch.bfloat16),) * 3)

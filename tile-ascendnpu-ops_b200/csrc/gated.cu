@@ -4,7 +4,7 @@
 // HBM-bound (3 * M * N * elem bytes per call).  The vector path gives each
 // thread a 16-byte packet of the gate half and the matching packet of the
 // value half (both coalesced across the warp, since packets of one warp are
-// consecutive columns of one row), computes in fp32 and rounds once.  Two
+// consecutive columns of one row), computes in fp32 and rounds once.  Four
 // packet pairs are kept in flight per thread.  Rows whose width N is not a
 // multiple of the packet, or misaligned pointers, take the scalar kernel.
 //
@@ -18,11 +18,48 @@ namespace tileops {
 namespace {
 
 constexpr int kThreads = 256;
+constexpr int kUnroll = 4;  // packet pairs in flight per thread
+
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// erf by Abramowitz & Stegun, Handbook of Mathematical Functions, formula
+// 7.1.26 (Hastings' rational approximation): for a = |x|,
+//   erf(a) = 1 - (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-a^2),
+//   t = 1 / (1 + p a),  |error| <= 1.5e-7,
+// and erf(-x) = -erf(x).  Branch-free: one reciprocal, one exp2, five FMAs,
+// where a library erf spends ~30 instructions across two divergent ranges.
+// Limits: erf(+-inf) = +-1 (t = 0, exp = 0) and NaN propagates.
+__device__ __forceinline__ float erf_as7126(float x) {
+  const float a = fabsf(x);
+  const float t = rcp_approx(fmaf(0.3275911f, a, 1.0f));
+  float poly = fmaf(t, 1.061405429f, -1.453152027f);
+  poly = fmaf(t, poly, 1.421413741f);
+  poly = fmaf(t, poly, -0.284496736f);
+  poly = fmaf(t, poly, 0.254829592f);
+  poly *= t;
+  const float e = ex2_approx(-(a * a) * 1.4426950408889634f);  // exp(-a^2)
+  return copysignf(fmaf(-poly, e, 1.0f), x);
+}
+
+// tanh(u) = 1 - 2 / (1 + exp(2u)); saturates to +-1 for large |u| and has an
+// absolute error of a few 1e-7, which GELU multiplies by 0.5 g.
+__device__ __forceinline__ float tanh_via_exp(float u) {
+  return fmaf(-2.0f, rcp_approx(1.0f + ex2_approx(u * 2.8853900817779268f)), 1.0f);
+}
 
 struct GeluErfF {
   __device__ __forceinline__ float operator()(float g, float v) const {
     // 0.5 * g * (1 + erf(g * sqrt(0.5))) * v, same association as the reference.
-    const float gelu = 0.5f * g * (1.0f + erff(g * 0.70710678118654752f));
+    const float gelu = 0.5f * g * (1.0f + erf_as7126(g * 0.70710678118654752f));
     return gelu * v;
   }
 };
@@ -31,7 +68,7 @@ struct GeluTanhF {
   __device__ __forceinline__ float operator()(float g, float v) const {
     // sqrt(2/pi) * (g + 0.044715 g^3), then 0.5 g (1 + tanh(inner)).
     const float inner = 0.79788456080286536f * (g + 0.044715f * (g * g * g));
-    const float gelu = 0.5f * g * (1.0f + tanhf(inner));
+    const float gelu = 0.5f * g * (1.0f + tanh_via_exp(inner));
     return gelu * v;
   }
 };
@@ -44,11 +81,11 @@ __global__ void __launch_bounds__(kThreads)
   const int64_t total = M * pk_per_row;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
   int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
-  for (; i + stride < total; i += 2 * stride) {
-    Pack16<T> g[2], v[2];
-    int64_t out_off[2];
+  for (; i + (kUnroll - 1) * stride < total; i += kUnroll * stride) {
+    Pack16<T> g[kUnroll], v[kUnroll];
+    int64_t out_off[kUnroll];
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
+    for (int u = 0; u < kUnroll; ++u) {
       const int64_t p = i + u * stride;
       const int64_t r = p / pk_per_row;
       const int64_t c = (p - r * pk_per_row) * V;
@@ -58,7 +95,7 @@ __global__ void __launch_bounds__(kThreads)
       out_off[u] = r * N + c;
     }
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
+    for (int u = 0; u < kUnroll; ++u) {
       Pack16<T> o;
 #pragma unroll
       for (int e = 0; e < V; ++e)
@@ -101,7 +138,7 @@ int launch_gated_t(const void* x, void* y, int64_t M, int64_t N, F f, cudaStream
   T* yp = static_cast<T*>(y);
   if (N % V == 0 && aligned16(x) && aligned16(y)) {
     const int64_t total = M * (N / V);
-    gated_vec<T, F><<<stream_grid(total, kThreads * 2, 8), kThreads, 0, s>>>(xp, yp, M, N, f);
+    gated_vec<T, F><<<stream_grid(total, kThreads * kUnroll, 8), kThreads, 0, s>>>(xp, yp, M, N, f);
   } else {
     gated_scalar<T, F><<<stream_grid(M * N, kThreads, 8), kThreads, 0, s>>>(xp, yp, M, N, f);
   }
