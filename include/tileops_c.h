@@ -164,6 +164,32 @@ int tileops_mha_fwd(const void* q, const void* k, const void* v, void* o, float*
                     int64_t seq_kv, int64_t dim, int is_causal, double sm_scale, int dtype,
                     void* stream);
 
+/* ---- gated delta net (linear attention) -------------------------------- */
+
+/* Bytes of scratch workspace tileops_gdn_prefill_fwd needs for this shape
+ * (per 64-token chunk of every (batch, head): the WY factors Wk (64 x dk),
+ * U (64 x dv) and the decayed causal q k^T (64 x 64) in bf16, plus 132 fp32),
+ * or -1 for an unsupported shape. */
+int64_t tileops_gdn_workspace_bytes(int64_t batch, int64_t seq_len, int64_t heads,
+                                    int64_t dim_k, int64_t dim_v);
+
+/* Gated delta rule, chunked prefill.  Per (b, h) and token t, with state S
+ * (dk x dv, fp32):  S <- exp(g_t) S;  S <- S + k_t (x) beta_t (v_t - k_t^T S);
+ * o_t = scale * q_t^T S.  Layout BTHD: q, k (B, T, H, dk) and v, o (B, T, H, dv)
+ * bf16; g (log decay), beta (B, T, H) fp32; initial_state (NULL = zeros) and
+ * final_state (NULL = not written) (B, H, dk, dv) fp32.  dk, dv in {64, 128};
+ * chunk_size must be 64; dtype must be TILEOPS_DT_BF16.  `workspace` holds
+ * tileops_gdn_workspace_bytes() bytes, 16-byte aligned, owned by the caller.
+ * The reference defines no op for this path (GatedDeltaNetPrefillFwdOp was not
+ * delivered); this entry replaces its probe kernel
+ * examples/gdn_prefill/probe/gdn_prefill_probe.py:83 and follows the
+ * sequential golden at :60-77. */
+int tileops_gdn_prefill_fwd(const void* q, const void* k, const void* v, const float* g,
+                            const float* beta, const float* initial_state, void* o,
+                            float* final_state, void* workspace, int64_t batch, int64_t seq_len,
+                            int64_t heads, int64_t dim_k, int64_t dim_v, int64_t chunk_size,
+                            double scale, int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -273,13 +273,22 @@ def main() -> None:
     # ---- GDN: the probe's sequential golden on the probe's own cases ----
     gold = src.function("examples/gdn_prefill/probe/gdn_prefill_probe.py",
                         "golden_gdn_sequential")
-    probe_cases = [(1, 2, 48, 16, 16), (2, 1, 48, 16, 16), (1, 1, 64, 32, 32),
-                   (1, 1, 192, 64, 64), (1, 1, 130, 128, 128)]
-    for bb, hh, tt, dd, dvv in probe_cases:
+    # The probe's own cases (head dim 16 / 32, its input distribution), plus
+    # head dims 64 / 128 with q, k L2-normalised: at those widths the probe's
+    # unnormalised k (|k|^2 ~ d / 4) makes (I - beta k k^T) expanding and the
+    # recurrence itself diverges, so the normalised form (the usual gated
+    # delta net input) is the meaningful case there.
+    probe_cases = [(1, 2, 48, 16, 16, False), (2, 1, 48, 16, 16, False),
+                   (1, 1, 64, 32, 32, False), (1, 1, 192, 64, 64, True),
+                   (1, 1, 130, 128, 128, True)]
+    for bb, hh, tt, dd, dvv, l2 in probe_cases:
         torch.manual_seed(0)  # the probe's seed (gdn_prefill_probe.py:_run_case)
         scale = dd**-0.5
-        q = (torch.randn(bb, hh, tt, dd) * 0.5).to(torch.float16)
-        k = (torch.randn(bb, hh, tt, dd) * 0.5).to(torch.float16)
+        q = torch.randn(bb, hh, tt, dd) * 0.5
+        k = torch.randn(bb, hh, tt, dd) * 0.5
+        if l2:
+            q, k = F.normalize(q, dim=-1), F.normalize(k, dim=-1)
+        q, k = q.to(torch.float16), k.to(torch.float16)
         v = (torch.randn(bb, hh, tt, dvv) * 0.5).to(torch.float16)
         g = (-torch.rand(bb, hh, tt) * 0.3).to(torch.float16)
         beta = torch.rand(bb, hh, tt).to(torch.float16)
@@ -288,7 +297,7 @@ def main() -> None:
         save(f"gdn_b{bb}_h{hh}_t{tt}_d{dd}_dv{dvv}", {"q": q, "k": k, "v": v, "g": g,
              "beta": beta, "state0": s0}, {"o": o, "final_state": s},
              {"source": "gdn_prefill_probe.py:golden_gdn_sequential", "layout": "BHTD",
-              "scale": scale, "seed": 0})
+              "scale": scale, "seed": 0, "qk_l2norm": l2})
 
 
 if __name__ == "__main__":

@@ -18,7 +18,7 @@ def test_library_loads():
 
 def test_every_declared_entry_point_is_exported():
     declared = _native.declared_entry_points()
-    assert len(declared) >= 16
+    assert len(declared) >= 18
     handle = _native.lib()
     missing = [name for name in declared if not hasattr(handle, name)]
     assert not missing, f"declared in include/tileops_c.h but not exported: {missing}"
@@ -90,3 +90,30 @@ def test_status_maps_to_python_exceptions():
         _native.call("tileops_hardswish_fwd", NULL, NULL, -5, 0, NULL)
     with pytest.raises(_native.NativeLibraryError):
         _native.call("tileops_no_such_entry")
+
+
+def test_gdn_workspace_and_validation():
+    lib = _native.lib()
+    assert lib.tileops_gdn_workspace_bytes(4, 8192, 16, 128, 128) == 4 * 16 * 128 * (
+        (64 * 128 + 64 * 128 + 64 * 64) * 2 + (2 * 64 + 4) * 4)
+    assert lib.tileops_gdn_workspace_bytes(1, 64, 1, 96, 128) == -1
+    args = [NULL] * 9
+    # chunk size other than 64
+    assert lib.tileops_gdn_prefill_fwd(*args, 1, 64, 1, 128, 128, 32, 0.1, 2, NULL) == (
+        _native.EBADSHAPE)
+    # fp16 is not supported
+    assert lib.tileops_gdn_prefill_fwd(*args, 1, 64, 1, 128, 128, 64, 0.1, 1, NULL) == (
+        _native.EBADDTYPE)
+    # NULL pointers
+    assert lib.tileops_gdn_prefill_fwd(*args, 1, 64, 1, 128, 128, 64, 0.1, 2, NULL) == (
+        _native.EINVAL)
+
+
+def test_mha_validation():
+    lib = _native.lib()
+    args = [NULL] * 5
+    assert lib.tileops_mha_fwd(*args, 1, 4, 3, 64, 64, 128, 0, 0.1, 2, NULL) == _native.EBADSHAPE
+    assert lib.tileops_mha_fwd(*args, 1, 4, 4, 64, 64, 96, 0, 0.1, 2, NULL) == _native.EBADSHAPE
+    assert lib.tileops_mha_fwd(*args, 1, 4, 4, 64, 64, 128, 0, 0.1, 0, NULL) == _native.EBADDTYPE
+    assert lib.tileops_mha_fwd(*args, 1, 4, 4, 128, 64, 128, 1, 0.1, 2, NULL) == (
+        _native.EBADSHAPE)

@@ -76,6 +76,7 @@ _SIGNATURES: dict[str, list] = {
     "tileops_conv1d_direct_fwd": [_p, _p, _p, _p] + [_i64] * 10 + [_i, _p],
     "tileops_mha_fwd": [_p, _p, _p, _p, _p] + [_i64] * 6 + [_i, _d, _i, _p],
     "tileops_gdn_prefill_fwd": [_p] * 9 + [_i64] * 6 + [_d, _i, _p],
+    "tileops_gdn_workspace_bytes": [_i64] * 5,
     "tileops_device_error_flag": [_p, _i],
     "tileops_abi_version": [],
     "tileops_status_string": [_i],
@@ -111,7 +112,10 @@ def lib() -> ctypes.CDLL:
                 if fn is None:
                     continue  # reported by declared_entry_points() checks
                 fn.argtypes = argtypes
-                fn.restype = ctypes.c_char_p if name == "tileops_status_string" else ctypes.c_int
+                fn.restype = {
+                    "tileops_status_string": ctypes.c_char_p,
+                    "tileops_gdn_workspace_bytes": ctypes.c_int64,
+                }.get(name, ctypes.c_int)
             _lib = handle
     return _lib
 
@@ -119,7 +123,9 @@ def lib() -> ctypes.CDLL:
 def declared_entry_points() -> list[str]:
     """Names of every function the C header declares."""
     text = _HEADER.read_text()
-    return sorted(set(re.findall(r"^\s*(?:int|const char\*)\s+(tileops_\w+)\s*\(", text, re.M)))
+    return sorted(
+        set(re.findall(r"^\s*(?:int|int64_t|const char\*)\s+(tileops_\w+)\s*\(", text, re.M))
+    )
 
 
 def dtype_code(dtype: torch.dtype) -> int:
