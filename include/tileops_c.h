@@ -190,6 +190,23 @@ int tileops_gdn_prefill_fwd(const void* q, const void* k, const void* v, const f
                             int64_t heads, int64_t dim_k, int64_t dim_v, int64_t chunk_size,
                             double scale, int dtype, void* stream);
 
+/* Same as tileops_gdn_prefill_fwd, but allocates nothing and takes no
+ * workspace: for callers that cannot allocate device memory when they call
+ * (inside a captured CUDA graph, or a host runtime / plugin without a device
+ * allocator).  The scratch is a fixed 16 MiB array in this library's device
+ * memory, held on every GPU that loads the library until exit; shapes needing
+ * more than that (tileops_gdn_workspace_bytes() > 16 MiB, i.e. more than 404
+ * chunks of 64 tokens summed over batch * heads at dk = dv = 128) return
+ * TILEOPS_EBADSHAPE before anything is enqueued.  All calls share the array,
+ * so calls whose kernels overlap on the GPU race.  The first call on a device
+ * looks up the array's device address; make it outside any stream capture.
+ * This entry point has no counterpart in the reference. */
+int tileops_gdn_prefill_fwd_noalloc(const void* q, const void* k, const void* v, const float* g,
+                                    const float* beta, const float* initial_state, void* o,
+                                    float* final_state, int64_t batch, int64_t seq_len,
+                                    int64_t heads, int64_t dim_k, int64_t dim_v,
+                                    int64_t chunk_size, double scale, int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

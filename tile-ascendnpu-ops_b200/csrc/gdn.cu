@@ -30,6 +30,8 @@
 // Layout: q, k (B, T, H, dk) bf16; v, o (B, T, H, dv) bf16; g, beta (B, T, H)
 // fp32; initial / final state (B, H, dk, dv) fp32.  Tokens past T are
 // treated as k = v = q = 0, g = beta = 0 (they leave the state unchanged).
+#include <mutex>
+
 #include "common.cuh"
 
 namespace tileops {
@@ -679,4 +681,66 @@ extern "C" int tileops_gdn_prefill_fwd(const void* q, const void* k, const void*
                                H, sc, s);
   return launch_gdn<64, 128>(q, k, v, g, beta, initial_state, o, final_state, workspace, B, T, H,
                              sc, s);
+}
+
+// ------------------------------------------------------------------------
+// No-allocation variant.
+//
+// Some callers cannot allocate device memory at call time: code running
+// inside a captured CUDA graph or an allocator-free runtime (a C host that
+// never links the CUDA allocator, a plugin that owns no memory pool, a
+// signal-safe or real-time path where cudaMalloc may block or fail).  For
+// them this entry point runs the same two kernels with the per-chunk WY
+// factors kept in a fixed scratch array that lives in the library's own
+// device memory instead of a caller-provided workspace.
+//
+// Limits and contract:
+//  * The scratch is kGdnStaticScratchBytes (16 MiB) per GPU, held by every GPU
+//    that loads this library until the process exits.  A shape needs
+//    tileops_gdn_workspace_bytes(...) bytes of it (41,488 bytes per 64-token
+//    chunk of every (batch, head) at dk = dv = 128, so at most 404 such
+//    chunks, e.g. batch * heads = 16 with seq_len <= 1,600); larger shapes are
+//    rejected with TILEOPS_EBADSHAPE before anything is enqueued.
+//  * All calls share the one array: two calls whose kernels overlap on the GPU
+//    (different streams, or different host threads) race on it.
+//  * Nothing in the scratch has to start at zero: the prepare kernel writes
+//    every byte the scan kernel reads for the chunks in use.
+//  * The device address of the array is looked up (cudaGetSymbolAddress) on
+//    the first call on each device, with that device current; make that first
+//    call outside any stream capture.
+constexpr size_t kGdnStaticScratchBytes = static_cast<size_t>(16) << 20;
+static __device__ __align__(256) unsigned char g_gdn_static_scratch[kGdnStaticScratchBytes];
+
+namespace {
+void* gdn_static_scratch_ptr() {
+  static std::mutex mu;
+  static void* cached[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!cached[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_gdn_static_scratch) != cudaSuccess) return nullptr;
+    cached[dev] = p;
+  }
+  return cached[dev];
+}
+}  // namespace
+
+extern "C" int tileops_gdn_prefill_fwd_noalloc(const void* q, const void* k, const void* v,
+                                               const float* g, const float* beta,
+                                               const float* initial_state, void* o,
+                                               float* final_state, int64_t batch,
+                                               int64_t seq_len, int64_t heads, int64_t dim_k,
+                                               int64_t dim_v, int64_t chunk_size, double scale,
+                                               int dtype, void* stream) {
+  const int64_t need = tileops_gdn_workspace_bytes(batch, seq_len, heads, dim_k, dim_v);
+  if (need < 0) return TILEOPS_EBADSHAPE;
+  if (static_cast<uint64_t>(need) > kGdnStaticScratchBytes) return TILEOPS_EBADSHAPE;
+  if (batch == 0 || seq_len == 0) return TILEOPS_OK;
+  void* scratch = gdn_static_scratch_ptr();
+  if (!scratch) return TILEOPS_ELAUNCH;
+  return tileops_gdn_prefill_fwd(q, k, v, g, beta, initial_state, o, final_state, scratch,
+                                 batch, seq_len, heads, dim_k, dim_v, chunk_size, scale, dtype,
+                                 stream);
 }

@@ -77,6 +77,7 @@ _SIGNATURES: dict[str, list] = {
     "tileops_mha_fwd": [_p, _p, _p, _p, _p] + [_i64] * 6 + [_i, _d, _i, _p],
     "tileops_gdn_prefill_fwd": [_p] * 9 + [_i64] * 6 + [_d, _i, _p],
     "tileops_gdn_workspace_bytes": [_i64] * 5,
+    "tileops_gdn_prefill_fwd_noalloc": [_p] * 8 + [_i64] * 6 + [_d, _i, _p],
     "tileops_device_error_flag": [_p, _i],
     "tileops_abi_version": [],
     "tileops_status_string": [_i],
