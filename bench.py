@@ -70,6 +70,7 @@ class Workload:
     # (GDN: metric TFLOP/s, bound HBM): work per step in that unit.
     roof_unit: Optional[str] = None
     roof_work_per_step: Optional[Callable[[object], float]] = None
+    launches_per_step: int = 1  # kernels of this library one step launches
     extra: dict = field(default_factory=dict)
 
 
@@ -103,7 +104,7 @@ def _faln() -> Workload:
                 "M": M, "N": N},
         make_inputs=make, build_op=lambda: FusedAddLayerNormFwdOp(dtype=torch.bfloat16),
         run=lambda op, inp: op(*inp), work_per_step=lambda op: float(op.eval_roofline()[1]),
-        kernel_regex="faln_rows", cpu_fn=cpu,
+        kernel_regex="faln_", cpu_fn=cpu,
         cpu_slice=lambda inp, rows: (inp[0][:rows], inp[1][:rows], inp[2], inp[3]),
         cpu_units=units,
     )
@@ -292,6 +293,7 @@ def _gdn() -> Workload:
         build_op=lambda: GatedDeltaNetPrefillFwdOp(B, T, H, DK, DV),
         run=lambda op, inp: op(*inp), work_per_step=lambda op: float(op.eval_roofline()[0]),
         kernel_regex="gdn_", cpu_fn=cpu, cpu_slice=sample, cpu_units=units,
+        launches_per_step=2,  # gdn_prepare + gdn_scan
     )
 
 
@@ -433,7 +435,18 @@ def barrier(world: int, device) -> None:
     if world > 1:
         import torch.distributed as dist
 
-        dist.barrier(device_ids=[device.index])
+        if device.type == "cuda":
+            dist.barrier(device_ids=[device.index])
+        else:  # gloo ranks (host-side tests of the multi-rank path)
+            dist.barrier()
+
+
+def whole_job_value(work_per_step: float, steps: int, total_ms: float, world: int,
+                    unit: str) -> float:
+    """Weak scaling: every rank ran ``steps`` steps of ``work_per_step`` units;
+    ``total_ms`` is the slowest rank's timed region."""
+    scale = 1e9 if unit == "GB/s" else 1e12
+    return world * work_per_step * steps / (total_ms * 1e-3) / scale
 
 
 # ---------------------------------------------------------------- our arm
@@ -536,7 +549,7 @@ def run_ours(args, wl: Workload) -> Optional[dict]:
     barrier(world, device)
 
     scale = 1e9 if wl.unit == "GB/s" else 1e12
-    value = world * work * args.steps / (total_ms * 1e-3) / scale
+    value = whole_job_value(work, args.steps, total_ms, world, wl.unit)
     roof_unit = wl.roof_unit or wl.unit
     roof_work = wl.roof_work_per_step(op) if wl.roof_work_per_step else work
     roof_scale = 1e9 if roof_unit == "GB/s" else 1e12
@@ -568,10 +581,10 @@ def run_ours(args, wl: Workload) -> Optional[dict]:
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json)" if peak_kind ==
                      "measured" else "fallback", "per_launch_ms": per_launch_ms,
                      "algorithmic_per_launch": roof_work},
-        "e2e": {"value": work / (e2e_ms * 1e-3) / scale, "unit": wl.unit,
+        "e2e": {"value": whole_job_value(work, 1, e2e_ms, world, wl.unit), "unit": wl.unit,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
                 "api": f"{type(op).__name__}.__call__ with pinned host buffers"},
-        "gpu_launches": args.steps,
+        "gpu_launches": args.steps * wl.launches_per_step,
         "clocks": clocks,
     }
     if world == 1 and not args.no_cpu_baseline and wl.cpu_fn is not None:
