@@ -12,7 +12,10 @@ batch, no collective on the data path).  MHA / GDN lines report TFLOP/s.
 
 Timing: W warm-up steps, then K steps bracketed by a barrier and
 ``torch.cuda.synchronize()``, CUDA events on the launching stream around
-every step, max over ranks.  Inputs rotate over enough distinct buffer sets
+every graph replay, max over ranks.  The K steps run as replays of a CUDA
+graph holding up to 64 consecutive op calls, each with its own outputs
+(``--no-graph``: K eager calls, which the host's Python cost can starve when
+a kernel is ~50 us).  Inputs rotate over enough distinct buffer sets
 that every step's working set was evicted from the 126 MB L2 (the set count
 is in ``config``).  ``e2e`` repeats the measurement through the public op API
 with pinned HOST buffers: H2D of the inputs, the op, D2H of the outputs.
@@ -500,20 +503,57 @@ def run_ours(args, wl: Workload) -> Optional[dict]:
         wl.run(op, sets[i % n_sets])
     torch.cuda.synchronize(device)
 
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    # Graph mode: a CUDA graph holds R consecutive op calls (validation,
+    # output allocation, the library's launches) over the rotating input
+    # sets, each call with outputs of its own; K steps replay it K // R times
+    # (plus a graph of the K % R remaining calls).  Eager mode calls the op
+    # K times from Python.
+    out_bytes = max(1, set_bytes - sum(t.numel() * t.element_size() for t in probe
+                                       if isinstance(t, torch.Tensor)))
+    per_graph = max(1, min(64, (8 << 30) // out_bytes) // n_sets) * n_sets
+    per_graph = min(per_graph, args.steps)
+
+    def capture(n):
+        graph = torch.cuda.CUDAGraph()
+        keep = []
+        with torch.cuda.graph(graph):
+            for i in range(n):
+                keep.append(wl.run(op, sets[i % n_sets]))
+        del keep
+        return graph
+
+    if args.graph:
+        g_main = capture(per_graph)
+        rem = args.steps % per_graph
+        g_rem = capture(rem) if rem else None
+        chunks = [(g_main.replay, per_graph)] * (args.steps // per_graph)
+        if g_rem is not None:
+            chunks.append((g_rem.replay, rem))
+        for _ in range(max(1, -(-args.warmup // per_graph))):
+            g_main.replay()
+        torch.cuda.synchronize(device)
+    else:
+        chunks = [((lambda inp=sets[i % n_sets]: wl.run(op, inp)), 1) for i in range(args.steps)]
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in chunks]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in chunks]
     sampler = ClockSampler(local_rank)
     barrier(world, device)
     torch.cuda.synchronize(device)
     with sampler:
-        for i in range(args.steps):
+        for i, (fn, _) in enumerate(chunks):
             starts[i].record(stream)
-            wl.run(op, sets[i % n_sets])
+            fn()
             ends[i].record(stream)
         torch.cuda.synchronize(device)
     barrier(world, device)
     total_ms = starts[0].elapsed_time(ends[-1])
-    per_launch_ms = statistics.mean(s.elapsed_time(e) for s, e in zip(starts, ends))
+    # Mean step time inside the timed calls (excludes host gaps between them).
+    per_launch_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / args.steps
+    chunk_steps = [n for _, n in chunks]
+    del chunks
+    if args.graph:
+        del g_main, g_rem
     total_ms = max_over_ranks(total_ms, world, device)
     per_launch_ms = max_over_ranks(per_launch_ms, world, device)
 
@@ -575,7 +615,10 @@ def run_ours(args, wl: Workload) -> Optional[dict]:
         "data": "synthetic (seeded torch.randn of the BASELINE shapes)",
         "config": {**wl.config, "parallelism": f"independent batch per GPU x{world}",
                    "l2": f"rotating {n_sets} input/output sets "
-                         f"({n_sets * set_bytes / 2**20:.0f} MiB) > 126 MB L2"},
+                         f"({n_sets * set_bytes / 2**20:.0f} MiB) > 126 MB L2",
+                   "timing": (f"CUDA-graph replays of {chunk_steps[0]} op calls each, "
+                              "CUDA events around each replay" if args.graph else
+                              "eager op calls, CUDA events per step")},
         "roofline": {"bound": wl.bound, "achieved": achieved, "peak": peak, "unit": peak_unit,
                      "frac": achieved / peak, "traffic": load_traffic(wl.name),
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json)" if peak_kind ==
@@ -637,6 +680,8 @@ def main() -> None:
     ap.add_argument("--ref-rows", type=int, default=256,
                     help="rows of the batch the CPU reference processes per step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", dest="graph", action="store_false",
+                    help="time eager op calls instead of CUDA-graph replays")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

@@ -245,3 +245,40 @@ def test_baseline_size_sampled():
     xi = torch.randint(-128, 128, shape, device="cuda", dtype=torch.int32)
     yi = BitwiseNotFwdOp(n, torch.int32)(xi)
     assert torch.equal(yi, ~xi)  # device-side exact check of every element
+
+
+# --------------------------------- every 16-bit encoding, bit for bit
+def _all_encodings(dtype):
+    return torch.arange(-32768, 32768, dtype=torch.int32).to(torch.int16).view(dtype)
+
+
+def _same_bits(y, expect):
+    """Equal encodings, any NaN matching any NaN (payloads are not part of the contract)."""
+    nan_y, nan_e = torch.isnan(y), torch.isnan(expect)
+    assert torch.equal(nan_y, nan_e)
+    keep = ~nan_e
+    assert torch.equal(y[keep].view(torch.int16), expect[keep].view(torch.int16))
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_all_16bit_inputs_bit_exact(dtype):
+    """Hardswish, hardsigmoid and clamp over all 65536 inputs equal the fp32
+    reference rounded once (the kernels divide by 6 as a multiply by RN(1/6)
+    on these types, which this pins)."""
+    x = _all_encodings(dtype)
+    xd = x.cuda()
+    n = x.numel()
+    _same_bits(HardswishFwdOp(n, dtype)(xd).cpu(), ref.hardswish(x))
+    _same_bits(HardsigmoidFwdOp(n, dtype)(xd).cpu(), ref.hardsigmoid(x))
+    _same_bits(ClampScalarFwdOp(n, dtype, min=-0.5, max=0.5)(xd).cpu(),
+               ref.clamp_scalar(x, -0.5, 0.5))
+    _same_bits(ClampScalarFwdOp(n, dtype, min=None, max=2.0)(xd).cpu(),
+               ref.clamp_scalar(x, None, 2.0))
+    _same_bits(ClampMinFwdOp(n, dtype, min=-1.0)(xd).cpu(), ref.clamp_scalar(x, -1.0, None))
+
+
+def test_clamp_nan_bound_propagates():
+    x = torch.randn(4096, device="cuda")
+    y = ClampScalarFwdOp(4096, torch.float32, min=float("nan"), max=1.0)(x).cpu()
+    expect = torch.clamp(x.cpu(), min=float("nan"), max=1.0)
+    assert torch.equal(torch.isnan(y), torch.isnan(expect))

@@ -42,6 +42,7 @@
 
 #include "common.cuh"
 #include "sm100.cuh"
+#include "tma_host.cuh"
 
 namespace tileops {
 namespace {
@@ -389,45 +390,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ------------------------------------------------------------------ host
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-  });
-  return fn;
-}
-
-// 4-D map over a BSHD tensor: dims (D, H, S, B), box (64, 1, 128, 1), 128B swizzle.
-bool make_map(CUtensorMap* map, const void* base, int dim, int heads, int seq, int batch,
-              bool bf16) {
-  auto fn = encode_fn();
-  if (!fn) return false;
-  cuuint64_t sizes[4] = {static_cast<cuuint64_t>(dim), static_cast<cuuint64_t>(heads),
-                         static_cast<cuuint64_t>(seq), static_cast<cuuint64_t>(batch)};
-  cuuint64_t strides[3] = {static_cast<cuuint64_t>(dim) * 2,
-                           static_cast<cuuint64_t>(dim) * heads * 2,
-                           static_cast<cuuint64_t>(dim) * heads * seq * 2};
-  cuuint32_t box[4] = {64, 1, 128, 1};
-  cuuint32_t estride[4] = {1, 1, 1, 1};
-  CUresult r = fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                  4, const_cast<void*>(base), sizes, strides, box, estride,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
-}
-
 template <int D, bool BF16>
 int launch_attn(const void* q, const void* k, const void* v, void* o, float* lse, int B, int H,
                 int Hkv, int Sq, int Skv, int causal, float sm_scale, cudaStream_t s) {
   CUtensorMap tq, tk, tv;
-  if (!make_map(&tq, q, D, H, Sq, B, BF16) || !make_map(&tk, k, D, Hkv, Skv, B, BF16) ||
-      !make_map(&tv, v, D, Hkv, Skv, B, BF16))
+  if (!make_bshd_map(&tq, q, D, H, Sq, B, 128, BF16) ||
+      !make_bshd_map(&tk, k, D, Hkv, Skv, B, 128, BF16) ||
+      !make_bshd_map(&tv, v, D, Hkv, Skv, B, 128, BF16))
     return TILEOPS_ELAUNCH;
   Params p;
   p.batch = B;

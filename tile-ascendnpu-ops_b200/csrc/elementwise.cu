@@ -23,30 +23,55 @@ constexpr int kThreads = 256;
 constexpr int kUnroll = 4;
 
 // ---------------------------------------------------------------- functors
+// NaN-propagating min / max (PTX min.NaN / max.NaN, sm_80+): a NaN operand
+// gives NaN, as torch's clamp / hardsigmoid do.
+__device__ __forceinline__ float fmax_nan(float a, float b) {
+  float d;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+  return d;
+}
+__device__ __forceinline__ float fmin_nan(float a, float b) {
+  float d;
+  asm("min.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+  return d;
+}
+
+// v / 6.  For fp16 and bf16 inputs, v * RN(1/6) rounds to the same 16-bit
+// result as RN32(v / 6) for every one of the 65536 input encodings (the
+// tests check all of them), so the 16-bit paths multiply; float32 output
+// keeps the IEEE division.
+template <bool kExactDiv>
+__device__ __forceinline__ float div6(float v) {
+  if constexpr (kExactDiv) {
+    return v / 6.0f;
+  } else {
+    return v * (1.0f / 6.0f);
+  }
+}
+
+template <bool kExactDiv>
 struct HardswishF {
   __device__ __forceinline__ float operator()(float x) const {
-    // x * min(max(x + 3, 0), 6) / 6, evaluated left to right like torch.
+    // x * min(max(x + 3, 0), 6) / 6, evaluated left to right like torch;
+    // a NaN x gives NaN through the product.
     const float t = fminf(fmaxf(x + 3.0f, 0.0f), 6.0f);
-    return x * t / 6.0f;
+    return div6<kExactDiv>(x * t);
   }
 };
 
+template <bool kExactDiv>
 struct HardsigmoidF {
   __device__ __forceinline__ float operator()(float x) const {
-    if (x != x) return x;  // NaN in -> NaN out (torch's maximum/minimum propagate it)
-    return fminf(fmaxf(x + 3.0f, 0.0f), 6.0f) / 6.0f;
+    return div6<kExactDiv>(fmin_nan(fmax_nan(x + 3.0f, 0.0f), 6.0f));
   }
 };
 
+// torch.clamp(x, lo, hi) = min(max(x, lo), hi) with NaN in x or in a bound
+// propagating; an absent bound is passed as -inf / +inf.
 struct ClampF {
   float lo, hi;
-  int has_lo, has_hi;
   __device__ __forceinline__ float operator()(float x) const {
-    float r = x;
-    // NaN in either operand propagates, as torch.clamp does.
-    if (has_lo) r = (r != r) ? r : ((lo != lo) ? lo : fmaxf(r, lo));
-    if (has_hi) r = (r != r) ? r : ((hi != hi) ? hi : fminf(r, hi));
-    return r;
+    return fmin_nan(fmax_nan(x, lo), hi);
   }
 };
 
@@ -105,16 +130,18 @@ int launch_map_t(const void* x, void* y, int64_t n, F f, cudaStream_t s) {
   return launch_status();
 }
 
-template <typename F>
-int launch_map(const void* x, void* y, int64_t n, int dtype, F f, void* stream) {
+// f32 runs f32_fn, the 16-bit types run half_fn.
+template <typename F32Fn, typename HalfFn>
+int launch_map(const void* x, void* y, int64_t n, int dtype, F32Fn f32_fn, HalfFn half_fn,
+               void* stream) {
   if (n < 0) return TILEOPS_EBADSHAPE;
   if (n == 0) return TILEOPS_OK;
   if (!x || !y) return TILEOPS_EINVAL;
   cudaStream_t s = as_stream(stream);
   switch (dtype) {
-    case TILEOPS_DT_F32: return launch_map_t<float>(x, y, n, f, s);
-    case TILEOPS_DT_F16: return launch_map_t<__half>(x, y, n, f, s);
-    case TILEOPS_DT_BF16: return launch_map_t<__nv_bfloat16>(x, y, n, f, s);
+    case TILEOPS_DT_F32: return launch_map_t<float>(x, y, n, f32_fn, s);
+    case TILEOPS_DT_F16: return launch_map_t<__half>(x, y, n, half_fn, s);
+    case TILEOPS_DT_BF16: return launch_map_t<__nv_bfloat16>(x, y, n, half_fn, s);
     default: return TILEOPS_EBADDTYPE;
   }
 }
@@ -285,21 +312,22 @@ using namespace tileops;
 
 extern "C" int tileops_hardswish_fwd(const void* x, void* y, int64_t n, int dtype,
                                      void* stream) {
-  return launch_map(x, y, n, dtype, HardswishF{}, stream);
+  return launch_map(x, y, n, dtype, HardswishF<true>{}, HardswishF<false>{}, stream);
 }
 
 extern "C" int tileops_hardsigmoid_fwd(const void* x, void* y, int64_t n, int dtype,
                                        void* stream) {
-  return launch_map(x, y, n, dtype, HardsigmoidF{}, stream);
+  return launch_map(x, y, n, dtype, HardsigmoidF<true>{}, HardsigmoidF<false>{}, stream);
 }
 
 extern "C" int tileops_clamp_scalar_fwd(const void* x, void* y, int64_t n, int dtype,
                                         int has_min, double min_val, int has_max,
                                         double max_val, void* stream) {
   if (!has_min && !has_max) return TILEOPS_EINVAL;
-  ClampF f{static_cast<float>(min_val), static_cast<float>(max_val), has_min ? 1 : 0,
-           has_max ? 1 : 0};
-  return launch_map(x, y, n, dtype, f, stream);
+  const float inf = __builtin_huge_valf();
+  const ClampF f{has_min ? static_cast<float>(min_val) : -inf,
+                 has_max ? static_cast<float>(max_val) : inf};
+  return launch_map(x, y, n, dtype, f, f, stream);
 }
 
 extern "C" int tileops_isnan_fwd(const void* x, void* y, int64_t n, int dtype, void* stream) {

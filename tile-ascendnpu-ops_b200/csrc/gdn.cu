@@ -16,16 +16,18 @@
 //   o       = scale e^gc (.) (Q S) + QKm err
 //   S_next  = e^gc_last S + K^T (e^(gc_last - gc) (.) err)
 //
-// Kernel 1 (gdn_prepare): one CTA per (b, h, chunk).  KK^T and QK^T on tensor
-// cores (mma.sync bf16, fp32 accumulate); T by 16 x 16 block forward
-// substitution in fp32 (diagonal blocks by substitution, off-diagonal blocks
-// by T_ij = -T_ii sum_m A_im T_mj); Wk and U as tensor-core products with T.
-// Results go to a caller-provided workspace, 64 x (dk + dv + 64) bf16 plus 64
-// fp32 per chunk.
+// Kernel 1 (gdn_prepare): one CTA per (b, h, chunk), K / Q / V by TMA.
+// KK^T and QK^T on tensor cores (mma.sync bf16, fp32 accumulate, lower
+// triangle only); T by 16 x 16 block forward substitution in fp32 (diagonal
+// blocks by substitution, off-diagonal blocks by T_ij = -T_ii sum_m A_im T_mj,
+// one warp per block); Wk = (T diag(beta e^gc)) K and U = (T diag(beta)) V as
+// tensor-core products.  Results go to a caller-provided workspace,
+// 64 x (dk + dv + 64) bf16 plus 132 fp32 per chunk.
 // Kernel 2 (gdn_scan): one CTA per (b, h, 64-wide slice of dv) -- the columns
 // of S evolve independently -- walking the chunks in order.  S lives in fp32
-// registers as MMA accumulators; every chunk's operands are prefetched one
-// chunk ahead with cp.async into padded (bank-conflict free) shared memory.
+// registers as MMA accumulators; one thread streams every chunk's operands
+// (q, k and the workspace tiles) one chunk ahead by TMA into swizzled shared
+// memory.
 //
 // Layout: q, k (B, T, H, dk) bf16; v, o (B, T, H, dv) bf16; g, beta (B, T, H)
 // fp32; initial / final state (B, H, dk, dv) fp32.  Tokens past T are
@@ -33,6 +35,8 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "sm100.cuh"
+#include "tma_host.cuh"
 
 namespace tileops {
 namespace {
@@ -42,11 +46,6 @@ constexpr int kC = 64;  // chunk length
 // ---------------------------------------------------- warp-level MMA helpers
 __device__ __forceinline__ uint32_t saddr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(saddr(p)));
 }
 __device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
@@ -62,19 +61,6 @@ __device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], 
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// A fragment (16 x 16) of a row-major [m][k] bf16 tile, rows m0.., cols k0..
-__device__ __forceinline__ void frag_a(uint32_t (&a)[4], const __nv_bfloat16* base, int ld,
-                                       int m0, int k0) {
-  const int lane = threadIdx.x & 31;
-  ldsm_x4(a, base + (m0 + (lane & 15)) * ld + k0 + ((lane >> 4) << 3));
-}
-// A fragment of A = X^T where X is stored row-major [k][m].
-__device__ __forceinline__ void frag_a_t(uint32_t (&a)[4], const __nv_bfloat16* base, int ld,
-                                         int m0, int k0) {
-  const int lane = threadIdx.x & 31;
-  const int mat = lane >> 3;  // 0: (m0,k0) 1: (m0+8,k0) 2: (m0,k0+8) 3: (m0+8,k0+8)
-  ldsm_x4_t(a, base + (k0 + (lane & 7) + ((mat >> 1) << 3)) * ld + m0 + ((mat & 1) << 3));
-}
 // B fragments of two adjacent n-tiles (n0.., n0+8..) where B[k][n] is stored
 // row-major [k][n]: b[0..1] for tile n0, b[2..3] for tile n0 + 8.
 __device__ __forceinline__ void frag_b_kn(uint32_t (&b)[4], const __nv_bfloat16* base, int ld,
@@ -83,33 +69,9 @@ __device__ __forceinline__ void frag_b_kn(uint32_t (&b)[4], const __nv_bfloat16*
   const int mat = lane >> 3;  // 0: (k0,n0) 1: (k0+8,n0) 2: (k0,n0+8) 3: (k0+8,n0+8)
   ldsm_x4_t(b, base + (k0 + (lane & 7) + ((mat & 1) << 3)) * ld + n0 + ((mat >> 1) << 3));
 }
-// B fragments of two adjacent n-tiles where B[k][n] = X[n][k], X row-major [n][k].
-__device__ __forceinline__ void frag_b_nk(uint32_t (&b)[4], const __nv_bfloat16* base, int ld,
-                                          int k0, int n0) {
-  const int lane = threadIdx.x & 31;
-  const int mat = lane >> 3;  // 0: (n0,k0) 1: (n0,k0+8) 2: (n0+8,k0) 3: (n0+8,k0+8)
-  ldsm_x4(b, base + (n0 + (lane & 7) + ((mat >> 1) << 3)) * ld + k0 + ((mat & 1) << 3));
-}
-
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&v);
-}
-
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr(dst)), "l"(src)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async16_zfill(void* dst, const void* src, bool valid) {
-  // src-size 0 writes 16 zero bytes (out-of-range token).
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(saddr(dst)), "l"(src),
-               "r"(valid ? 16 : 0)
-               : "memory");
-}
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 // Workspace of one chunk (element offsets into a bf16 array, then fp32 tail).
@@ -128,45 +90,91 @@ struct Ws {
 };
 
 // =========================================================== kernel 1
-// 128 threads.  Shared memory (bf16 tiles padded by 8 columns):
-//   Ks [64][DK+8] (later overwritten in place by Kp = beta e^gc K),
-//   Qs [64][DK+8] (later reused for Ts, T in bf16 [64][72]),
-//   Vs [64][DV+8] (later overwritten in place by Vp = beta V),
-//   As, Tf: fp32 [64][65]; gc, beta: [64].
+// 128 threads (4 warps), one CTA per (b, h, chunk); three CTAs per SM.
+// K, Q, V arrive by TMA as 128-byte-swizzled [64][64] bf16 boxes (tokens
+// past T read as zeros).  Shared memory:
+//   Ks [64][DK], Vs [64][DV]   swizzled bf16 (TMA)
+//   Qs [64][DK]                swizzled bf16 (TMA); once QK^T is formed the
+//                              region holds Tf (T in fp32, [64][68]) and then
+//                              Tk, Tv (swizzled bf16 [64][64] each)
+//   As fp32 [64][65]           A, strictly lower
+//   gc, beta, ke = beta e^gc   [64] each
+//   mbarrier + abort flag
+// Tile addressing: 16-byte unit u of row r in a 64-column box at
+// ((u ^ (r & 7)) << 4), boxes 8 KB apart.
+__device__ __forceinline__ uint32_t swz(int r, int col) {  // col % 8 == 0
+  return ((col >> 6) << 13) + (r << 7) + ((((col & 63) >> 3) ^ (r & 7)) << 4);
+}
+__device__ __forceinline__ void ldsm4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm4t(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+// The four fragment loaders of the padded tiles, for swizzled tiles at
+// shared address `base` (same lane -> (row, column) assignment).
+__device__ __forceinline__ void sfrag_a(uint32_t (&a)[4], uint32_t base, int m0, int k0) {
+  const int lane = threadIdx.x & 31;
+  ldsm4(a, base + swz(m0 + (lane & 15), k0 + ((lane >> 4) << 3)));
+}
+__device__ __forceinline__ void sfrag_a_t(uint32_t (&a)[4], uint32_t base, int m0, int k0) {
+  const int lane = threadIdx.x & 31, mat = lane >> 3;
+  ldsm4t(a, base + swz(k0 + (lane & 7) + ((mat >> 1) << 3), m0 + ((mat & 1) << 3)));
+}
+__device__ __forceinline__ void sfrag_b_kn(uint32_t (&b)[4], uint32_t base, int k0, int n0) {
+  const int lane = threadIdx.x & 31, mat = lane >> 3;
+  ldsm4t(b, base + swz(k0 + (lane & 7) + ((mat & 1) << 3), n0 + ((mat >> 1) << 3)));
+}
+__device__ __forceinline__ void sfrag_b_nk(uint32_t (&b)[4], uint32_t base, int k0, int n0) {
+  const int lane = threadIdx.x & 31, mat = lane >> 3;
+  ldsm4(b, base + swz(n0 + (lane & 7) + ((mat >> 1) << 3), k0 + ((mat & 1) << 3)));
+}
+
+constexpr int kLdTf = 68;  // fp32 row stride of Tf (16-byte aligned rows)
+constexpr int kLdA = 65;   // fp32 row stride of As
+
 template <int DK, int DV>
 struct PrepSmem {
-  static constexpr int kLdK = DK + 8, kLdV = DV + 8, kLdT = kC + 8, kLdF = kC + 1;
+  static constexpr int cmax(int a, int b) { return a > b ? a : b; }
   static constexpr int kKs = 0;
-  static constexpr int kQs = kKs + kC * kLdK * 2;
-  static constexpr int kVs = kQs + kC * kLdK * 2;
-  static constexpr int kAs = kVs + kC * kLdV * 2;
-  static constexpr int kTf = kAs + kC * kLdF * 4;
-  static constexpr int kGc = kTf + kC * kLdF * 4;
+  static constexpr int kQs = kKs + kC * DK * 2;
+  static constexpr int kQsBytes = cmax(cmax(kC * DK * 2, kC * kLdTf * 4), 2 * kC * kC * 2);
+  static constexpr int kVs = (kQs + kQsBytes + 1023) & ~1023;
+  static constexpr int kAs = kVs + kC * DV * 2;
+  static constexpr int kGc = kAs + kC * kLdA * 4;
   static constexpr int kBeta = kGc + kC * 4;
-  static constexpr int kBytes = kBeta + kC * 4;
+  static constexpr int kKe = kBeta + kC * 4;
+  static constexpr int kBar = kKe + kC * 4;
+  static constexpr int kBytes = kBar + 16;
+  static constexpr int kAlloc = kBytes + 1024;  // room to align the base to 1 KB
 };
 
 template <int DK, int DV>
-__global__ void __launch_bounds__(128)
-    gdn_prepare(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
-                const __nv_bfloat16* __restrict__ v, const float* __restrict__ g,
+__global__ void __launch_bounds__(128, 3)
+    gdn_prepare(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                const __grid_constant__ CUtensorMap tm_v, const float* __restrict__ g,
                 const float* __restrict__ beta, __nv_bfloat16* __restrict__ ws, int T, int H,
-                int nchunks, float scale) {
+                int nchunks, float scale, int* err) {
   using L = PrepSmem<DK, DV>;
   using W = Ws<DK, DV>;
-  extern __shared__ __align__(16) uint8_t sm[];
-  __nv_bfloat16* Ks = reinterpret_cast<__nv_bfloat16*>(sm + L::kKs);
-  __nv_bfloat16* Qs = reinterpret_cast<__nv_bfloat16*>(sm + L::kQs);
-  __nv_bfloat16* Vs = reinterpret_cast<__nv_bfloat16*>(sm + L::kVs);
-  __nv_bfloat16* Kp = Ks;  // in place, once KK^T is done
-  __nv_bfloat16* Vp = Vs;
-  __nv_bfloat16* Ts = Qs;  // once QK^T is done
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const uint32_t sb = saddr(sm);
   float* As = reinterpret_cast<float*>(sm + L::kAs);
-  float* Tf = reinterpret_cast<float*>(sm + L::kTf);
+  float* Tf = reinterpret_cast<float*>(sm + L::kQs);
   float* gc = reinterpret_cast<float*>(sm + L::kGc);
   float* bt = reinterpret_cast<float*>(sm + L::kBeta);
+  float* ke = reinterpret_cast<float*>(sm + L::kKe);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + L::kBar);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + L::kBar + 8);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g8 = lane >> 2, t2 = (lane & 3) * 2;
   const int chunk = blockIdx.x % nchunks;
   const int bh = blockIdx.x / nchunks;
   const int b = bh / H, h = bh - (bh / H) * H;
@@ -174,25 +182,22 @@ __global__ void __launch_bounds__(128)
   __nv_bfloat16* wsc = ws + static_cast<int64_t>(blockIdx.x) * (W::kBytes / 2);
   float* wsf = reinterpret_cast<float*>(wsc);
 
-  // ---- load K, Q, V rows of the chunk (zero past T) and g, beta
-  {
-    constexpr int kPkK = DK / 8, kPkV = DV / 8;  // 16-byte packets per row
-    for (int i = tid; i < kC * kPkK; i += 128) {
-      const int r = i / kPkK, c = (i - r * kPkK) * 8;
-      const int t = t0 + r;
-      const bool ok = t < T;
-      const int64_t off = ((static_cast<int64_t>(b) * T + (ok ? t : 0)) * H + h) * DK + c;
-      cp_async16_zfill(Ks + r * L::kLdK + c, k + off, ok);
-      cp_async16_zfill(Qs + r * L::kLdK + c, q + off, ok);
+  if (tid == 0) {
+    sm100::mbar_init(bar, 1);
+    *abort_flag = 0;
+    sm100::fence_mbar_init();
+  }
+  __syncthreads();
+  if (tid == 0) {
+    sm100::mbar_arrive_expect_tx(bar, (2 * DK + DV) * kC * 2);
+#pragma unroll
+    for (int c = 0; c < DK / 64; ++c) {
+      sm100::tma_load_4d(sm + L::kKs + c * 8192, &tm_k, bar, c * 64, h, t0, b);
+      sm100::tma_load_4d(sm + L::kQs + c * 8192, &tm_q, bar, c * 64, h, t0, b);
     }
-    for (int i = tid; i < kC * kPkV; i += 128) {
-      const int r = i / kPkV, c = (i - r * kPkV) * 8;
-      const int t = t0 + r;
-      const bool ok = t < T;
-      const int64_t off = ((static_cast<int64_t>(b) * T + (ok ? t : 0)) * H + h) * DV + c;
-      cp_async16_zfill(Vs + r * L::kLdV + c, v + off, ok);
-    }
-    cp_commit();
+#pragma unroll
+    for (int c = 0; c < DV / 64; ++c)
+      sm100::tma_load_4d(sm + L::kVs + c * 8192, &tm_v, bar, c * 64, h, t0, b);
   }
   if (warp == 0) {
     // inclusive cumsum of g over the 64 tokens: two per lane + warp scan
@@ -208,7 +213,7 @@ __global__ void __launch_bounds__(128)
       g1 = g[o];
       b1 = beta[o];
     }
-    float pair = g0 + g1;
+    const float pair = g0 + g1;
     float incl = pair;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -221,153 +226,195 @@ __global__ void __launch_bounds__(128)
     bt[2 * lane] = b0;
     bt[2 * lane + 1] = b1;
   }
-  cp_wait<0>();
-  __syncthreads();
+  // Every thread waits for the tiles (bounded); the CTA proceeds only if all
+  // saw them land, otherwise it lets any copy in flight finish and leaves.
+  const bool landed = sm100::mbar_wait(bar, 0, err, abort_flag);
+  if (!__syncthreads_and(landed)) {
+    if (tid == 0) sm100::mbar_wait(bar, 0, nullptr, abort_flag, true);
+    __syncthreads();
+    return;
+  }
+  const uint32_t sK = sb + L::kKs, sQ = sb + L::kQs, sV = sb + L::kVs;
 
-  // ---- KK^T -> A (strictly lower, fp32) and QK^T -> QKm (bf16, to workspace)
+  // ---- KK^T -> A (strictly lower, fp32) and QK^T -> QKm (lower, bf16, to the
+  // workspace); warp w owns rows 16w..16w+15 and only needs columns <= them.
   {
     const int m0 = warp * 16;
-    const int g8 = lane >> 2, t2 = (lane & 3) * 2;
+    const int ntiles = 2 * (warp + 1);
+    float ak[8][4], aq[8][4];
 #pragma unroll
-    for (int which = 0; which < 2; ++which) {
-      const __nv_bfloat16* X = which == 0 ? Ks : Qs;
-      float acc[8][4];
+    for (int n = 0; n < 8; ++n)
 #pragma unroll
-      for (int n = 0; n < 8; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
+      for (int e = 0; e < 4; ++e) ak[n][e] = aq[n][e] = 0.0f;
 #pragma unroll
-      for (int kk = 0; kk < DK / 16; ++kk) {
-        uint32_t a[4];
-        frag_a(a, X, L::kLdK, m0, kk * 16);
+    for (int kk = 0; kk < DK / 16; ++kk) {
+      uint32_t fk[4], fq[4];
+      sfrag_a(fk, sK, m0, kk * 16);
+      sfrag_a(fq, sQ, m0, kk * 16);
 #pragma unroll
-        for (int n = 0; n < 8; n += 2) {
+      for (int n = 0; n < 8; n += 2) {
+        if (n < ntiles) {
           uint32_t bb[4];
-          frag_b_nk(bb, Ks, L::kLdK, kk * 16, n * 8);
-          mma_bf16(acc[n], a, bb[0], bb[1]);
-          mma_bf16(acc[n + 1], a, bb[2], bb[3]);
+          sfrag_b_nk(bb, sK, kk * 16, n * 8);
+          mma_bf16(ak[n], fk, bb[0], bb[1]);
+          mma_bf16(ak[n + 1], fk, bb[2], bb[3]);
+          mma_bf16(aq[n], fq, bb[0], bb[1]);
+          mma_bf16(aq[n + 1], fq, bb[2], bb[3]);
         }
       }
+    }
 #pragma unroll
-      for (int n = 0; n < 8; ++n)
+    for (int half = 0; half < 2; ++half) {
+      const int l = m0 + g8 + half * 8;
+      const float gl = gc[l], bl = bt[l];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int l = m0 + g8 + ((e >> 1) << 3), s = n * 8 + t2 + (e & 1);
-          const float dec = __expf(gc[l] - gc[s]);
-          if (which == 0) {
-            As[l * L::kLdF + s] = l > s ? bt[l] * dec * acc[n][e] : 0.0f;
-          } else {
-            wsc[W::kQK + l * kC + s] = __float2bfloat16_rn(l >= s ? scale * dec * acc[n][e] : 0.0f);
-          }
-        }
+      for (int n = 0; n < 8; ++n) {
+        const int s = n * 8 + t2;
+        const float d0 = s <= l ? __expf(gl - gc[s]) : 0.0f;
+        const float d1 = s + 1 <= l ? __expf(gl - gc[s + 1]) : 0.0f;
+        As[l * kLdA + s] = s < l ? bl * d0 * ak[n][half * 2] : 0.0f;
+        As[l * kLdA + s + 1] = s + 1 < l ? bl * d1 * ak[n][half * 2 + 1] : 0.0f;
+        *reinterpret_cast<uint32_t*>(wsc + W::kQK + l * kC + s) =
+            pack_bf16(scale * d0 * aq[n][half * 2], scale * d1 * aq[n][half * 2 + 1]);
+      }
     }
   }
-  __syncthreads();
+  __syncthreads();  // As complete; the Qs region is free for Tf
 
-  // ---- in place: Kp = beta e^gc K, Vp = beta V; the fp32 tail of the workspace
-  {
-    const float gl = gc[kC - 1];
-    for (int i = tid; i < kC * DK; i += 128) {
-      const int r = i / DK, c = i - r * DK;
-      Kp[r * L::kLdK + c] =
-          __float2bfloat16_rn(bt[r] * __expf(gc[r]) * __bfloat162float(Ks[r * L::kLdK + c]));
-    }
-    for (int i = tid; i < kC * DV; i += 128) {
-      const int r = i / DV, c = i - r * DV;
-      Vp[r * L::kLdV + c] = __float2bfloat16_rn(bt[r] * __bfloat162float(Vs[r * L::kLdV + c]));
-    }
-    if (tid < kC) {
-      wsf[W::kQsc + tid] = scale * __expf(gc[tid]);
-      wsf[W::kDec + tid] = __expf(gl - gc[tid]);
-    }
-    if (tid < 4) wsf[W::kEgl + tid] = tid == 0 ? __expf(gl) : 0.0f;
-  }
-
-  // ---- T = (I + A)^-1, 16 x 16 blocks, fp32
-  // (1) diagonal blocks by forward substitution: thread (blk, col) owns one column.
-  if (tid < kC) {
+  // ---- diagonal 16 x 16 blocks of T = (I + A)^-1 by forward substitution
+  // (threads 0..63: one column each); threads 64..127 write the fp32 tail
+  // of the workspace and ke = beta e^gc.
+  if (tid < 64) {
     const int blk = tid >> 4, col = tid & 15, base = blk * 16;
     float t[16];
 #pragma unroll
     for (int l = 0; l < 16; ++l) {
       float acc = 0.0f;
 #pragma unroll
-      for (int m = 0; m < l; ++m) acc = fmaf(As[(base + l) * L::kLdF + base + m], t[m], acc);
+      for (int m = 0; m < l; ++m) acc = fmaf(As[(base + l) * kLdA + base + m], t[m], acc);
       t[l] = (l == col) ? 1.0f : (l > col ? -acc : 0.0f);
     }
 #pragma unroll
-    for (int l = 0; l < 16; ++l) Tf[(base + l) * L::kLdF + base + col] = t[l];
-  }
-  // zero the strictly upper blocks
-  for (int i = tid; i < kC * kC; i += 128) {
-    const int r = i >> 6, c = i & 63;
-    if ((c >> 4) > (r >> 4)) Tf[r * L::kLdF + c] = 0.0f;
-  }
-  __syncthreads();
-  // (2) off-diagonal blocks, by distance d = i - j = 1, 2, 3:
-  //     T_ij = -T_ii (sum_{m=j}^{i-1} A_im T_mj); 16 x 16 x 16 products on CUDA cores.
-  for (int d = 1; d < 4; ++d) {
-    const int nblocks = 4 - d;  // pairs (i, j = i - d)
-    // step a: X_ij = sum_m A_im T_mj  -> stored in As block (i, j) (A_ij no longer needed)
-    for (int e = tid; e < nblocks * 256; e += 128) {
-      const int pidx = e >> 8, rc = e & 255, r = rc >> 4, c = rc & 15;
-      const int i = pidx + d, j = pidx;
-      float acc = 0.0f;
-      for (int m = j; m < i; ++m)
-#pragma unroll
-        for (int x = 0; x < 16; ++x)
-          acc = fmaf(As[(i * 16 + r) * L::kLdF + m * 16 + x], Tf[(m * 16 + x) * L::kLdF + j * 16 + c],
-                     acc);
-      Tf[(i * 16 + r) * L::kLdF + j * 16 + c] = acc;  // temporarily X_ij
-    }
-    __syncthreads();
-    // step b: T_ij = -T_ii X_ij (read X from Tf, write result back after a barrier)
-    float res[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // (4 - d) * 256 / 128 <= 6 per thread
-    int cnt = 0;
-    for (int e = tid; e < nblocks * 256; e += 128, ++cnt) {
-      const int pidx = e >> 8, rc = e & 255, r = rc >> 4, c = rc & 15;
-      const int i = pidx + d, j = pidx;
-      float acc = 0.0f;
-#pragma unroll
-      for (int x = 0; x < 16; ++x)
-        acc = fmaf(Tf[(i * 16 + r) * L::kLdF + i * 16 + x], Tf[(i * 16 + x) * L::kLdF + j * 16 + c],
-                   acc);
-      res[cnt] = -acc;
-    }
-    __syncthreads();
-    cnt = 0;
-    for (int e = tid; e < nblocks * 256; e += 128, ++cnt) {
-      const int pidx = e >> 8, rc = e & 255, r = rc >> 4, c = rc & 15;
-      const int i = pidx + d, j = pidx;
-      Tf[(i * 16 + r) * L::kLdF + j * 16 + c] = res[cnt];
-    }
-    __syncthreads();
-  }
-  for (int i = tid; i < kC * kC; i += 128) {
-    const int r = i >> 6, c = i & 63;
-    Ts[r * L::kLdT + c] = __float2bfloat16_rn(Tf[r * L::kLdF + c]);
+    for (int l = 0; l < 16; ++l) Tf[(base + l) * kLdTf + base + col] = t[l];
+  } else {
+    const int i = tid - 64;
+    const float gl = gc[kC - 1];
+    const float e = __expf(gc[i]);
+    ke[i] = bt[i] * e;
+    wsf[W::kQsc + i] = scale * e;
+    wsf[W::kDec + i] = __expf(gl - gc[i]);
+    if (i < 4) wsf[W::kEgl + i] = i == 0 ? __expf(gl) : 0.0f;
   }
   __syncthreads();
 
-  // ---- Wk = T Kp (C x DK), U = T Vp (C x DV): warp w owns rows 16w..16w+15
+  // ---- off-diagonal blocks by distance d = i - j: warp p < 4 - d forms
+  //   X = sum_{m=j}^{i-1} A_im T_mj,   T_ij = -T_ii X      ((i, j) = (p + d, p))
+  // in fp32 on the CUDA cores; lane -> row lane / 2, columns 8 (lane % 2)...
+  for (int d = 1; d < 4; ++d) {
+    if (warp < 4 - d) {
+      const int i = warp + d, j = warp;
+      const int r = lane >> 1, c0 = j * 16 + (lane & 1) * 8;
+      float x[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) x[e] = 0.0f;
+      for (int m = j; m < i; ++m) {
+#pragma unroll
+        for (int kx = 0; kx < 16; ++kx) {
+          const float a = As[(i * 16 + r) * kLdA + m * 16 + kx];
+          const float4 u = *reinterpret_cast<const float4*>(Tf + (m * 16 + kx) * kLdTf + c0);
+          const float4 w = *reinterpret_cast<const float4*>(Tf + (m * 16 + kx) * kLdTf + c0 + 4);
+          x[0] = fmaf(a, u.x, x[0]);
+          x[1] = fmaf(a, u.y, x[1]);
+          x[2] = fmaf(a, u.z, x[2]);
+          x[3] = fmaf(a, u.w, x[3]);
+          x[4] = fmaf(a, w.x, x[4]);
+          x[5] = fmaf(a, w.y, x[5]);
+          x[6] = fmaf(a, w.z, x[6]);
+          x[7] = fmaf(a, w.w, x[7]);
+        }
+      }
+      float* xo = Tf + (i * 16 + r) * kLdTf + c0;  // block (i, j) holds X for now
+      *reinterpret_cast<float4*>(xo) = make_float4(x[0], x[1], x[2], x[3]);
+      *reinterpret_cast<float4*>(xo + 4) = make_float4(x[4], x[5], x[6], x[7]);
+      __syncwarp();
+      float y[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) y[e] = 0.0f;
+#pragma unroll
+      for (int kx = 0; kx < 16; ++kx) {
+        const float a = Tf[(i * 16 + r) * kLdTf + i * 16 + kx];
+        const float4 u = *reinterpret_cast<const float4*>(Tf + (i * 16 + kx) * kLdTf + c0);
+        const float4 w = *reinterpret_cast<const float4*>(Tf + (i * 16 + kx) * kLdTf + c0 + 4);
+        y[0] = fmaf(a, u.x, y[0]);
+        y[1] = fmaf(a, u.y, y[1]);
+        y[2] = fmaf(a, u.z, y[2]);
+        y[3] = fmaf(a, u.w, y[3]);
+        y[4] = fmaf(a, w.x, y[4]);
+        y[5] = fmaf(a, w.y, y[5]);
+        y[6] = fmaf(a, w.z, y[6]);
+        y[7] = fmaf(a, w.w, y[7]);
+      }
+      __syncwarp();
+      *reinterpret_cast<float4*>(xo) = make_float4(-y[0], -y[1], -y[2], -y[3]);
+      *reinterpret_cast<float4*>(xo + 4) = make_float4(-y[4], -y[5], -y[6], -y[7]);
+    }
+    __syncthreads();
+  }
+
+  // ---- Tk = T diag(beta e^gc), Tv = T diag(beta) in bf16, swizzled [64][64]
+  // each, over the Tf region (read all of Tf first).
+  {
+    const int l = tid >> 1, s0 = (tid & 1) * 32;
+    float tv[32];
+#pragma unroll
+    for (int q4 = 0; q4 < 8; ++q4) {
+      const float4 u = *reinterpret_cast<const float4*>(Tf + l * kLdTf + s0 + q4 * 4);
+      tv[q4 * 4 + 0] = u.x;
+      tv[q4 * 4 + 1] = u.y;
+      tv[q4 * 4 + 2] = u.z;
+      tv[q4 * 4 + 3] = u.w;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      uint4 pk, pv;
+      uint32_t* pkw = reinterpret_cast<uint32_t*>(&pk);
+      uint32_t* pvw = reinterpret_cast<uint32_t*>(&pv);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int s = s0 + c * 8 + 2 * e;
+        const float v0 = s <= l ? tv[c * 8 + 2 * e] : 0.0f;
+        const float v1 = s + 1 <= l ? tv[c * 8 + 2 * e + 1] : 0.0f;
+        pkw[e] = pack_bf16(v0 * ke[s], v1 * ke[s + 1]);
+        pvw[e] = pack_bf16(v0 * bt[s], v1 * bt[s + 1]);
+      }
+      *reinterpret_cast<uint4*>(sm + L::kQs + swz(l, s0 + c * 8)) = pk;
+      *reinterpret_cast<uint4*>(sm + L::kQs + 8192 + swz(l, s0 + c * 8)) = pv;
+    }
+  }
+  __syncthreads();
+
+  // ---- Wk = Tk K (C x DK), U = Tv V (C x DV): warp w owns rows 16w..16w+15;
+  // T is lower triangular, so k-blocks 0..w.
   {
     const int m0 = warp * 16;
-    const int g8 = lane >> 2, t2 = (lane & 3) * 2;
 #pragma unroll
     for (int which = 0; which < 2; ++which) {
       const int D = which == 0 ? DK : DV;
-      const int ld = which == 0 ? L::kLdK : L::kLdV;
-      const __nv_bfloat16* X = which == 0 ? Kp : Vp;
+      const uint32_t tA = sb + L::kQs + which * 8192;
+      const uint32_t X = which == 0 ? sK : sV;
       __nv_bfloat16* out = wsc + (which == 0 ? W::kWk : W::kU);
       for (int n0 = 0; n0 < D; n0 += 64) {
         float acc[8][4];
 #pragma unroll
         for (int n = 0; n < 8; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
-        for (int kk = 0; kk <= warp; ++kk) {  // T is lower triangular
+        for (int kk = 0; kk <= warp; ++kk) {
           uint32_t a[4];
-          frag_a(a, Ts, L::kLdT, m0, kk * 16);
+          sfrag_a(a, tA, m0, kk * 16);
 #pragma unroll
           for (int n = 0; n < 8; n += 2) {
             uint32_t bb[4];
-            frag_b_kn(bb, X, ld, kk * 16, n0 + n * 8);
+            sfrag_b_kn(bb, X, kk * 16, n0 + n * 8);
             mma_bf16(acc[n], a, bb[0], bb[1]);
             mma_bf16(acc[n + 1], a, bb[2], bb[3]);
           }
@@ -384,38 +431,48 @@ __global__ void __launch_bounds__(128)
 }
 
 // =========================================================== kernel 2
-// 256 threads (8 warps), one CTA per (b, h, 64-column slice of dv).
-// Per-stage shared memory (padded bf16): Qs, Ks, Wks [64][DK+8];
-// Us [64][72] (the slice); QKs [64][72]; eg [64] + gl.  Two stages.
-// Plus Ss [DK][72] (S in bf16, B operand), Es / Ed [64][72] (err and
-// decayed err, B operands).
+// 256 threads (8 warps), one CTA per (b, h, 64-column slice of dv), walking
+// the chunks in order.  Thread 0 streams every chunk's operands one chunk
+// ahead by TMA into two stages of 128-byte-swizzled tiles:
+//   Qs, Ks, Wks [64][DK]; Us [64][64] (the slice of U); QKs [64][64];
+//   the workspace's fp32 tail (a plain bulk copy).
+// Besides the stages: Ss [DK][72] (S in bf16, the B operand of Wk S and
+// Q S), Es / Ed [64][72] (err and decayed err, B operands), padded.
 constexpr int kSlice = 64;
 
 template <int DK>
 struct ScanSmem {
-  static constexpr int kLdK = DK + 8, kLdS = kSlice + 8;
+  static constexpr int kLdS = kSlice + 8;
   static constexpr int kQs = 0;
-  static constexpr int kKs = kQs + kC * kLdK * 2;
-  static constexpr int kWks = kKs + kC * kLdK * 2;
-  static constexpr int kUs = kWks + kC * kLdK * 2;
-  static constexpr int kQKs = kUs + kC * kLdS * 2;
-  static constexpr int kEg = kQKs + kC * kLdS * 2;  // the workspace fp32 tail
-  static constexpr int kStage = kEg + (2 * kC + 4) * 4;
+  static constexpr int kKs = kQs + kC * DK * 2;
+  static constexpr int kWks = kKs + kC * DK * 2;
+  static constexpr int kUs = kWks + kC * DK * 2;
+  static constexpr int kQKs = kUs + kC * kSlice * 2;
+  static constexpr int kEg = kQKs + kC * kC * 2;  // the workspace fp32 tail
+  static constexpr int kTailBytes = (2 * kC + 4) * 4;
+  static constexpr int kStage = (kEg + kTailBytes + 1023) & ~1023;
+  static constexpr int kLoadBytes = 3 * kC * DK * 2 + kC * kSlice * 2 + kC * kC * 2 + kTailBytes;
   static constexpr int kSs = 2 * kStage;
   static constexpr int kEs = kSs + DK * kLdS * 2;
   static constexpr int kEd = kEs + kC * kLdS * 2;
-  static constexpr int kBytes = kEd + kC * kLdS * 2;
+  static constexpr int kBar = kEd + kC * kLdS * 2;  // full[2] + abort flag
+  static constexpr int kBytes = kBar + 32;
+  static constexpr int kAlloc = kBytes + 1024;
 };
 
 template <int DK, int DV>
 __global__ void __launch_bounds__(256, 1)
-    gdn_scan(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
-             const __nv_bfloat16* __restrict__ ws, const float* __restrict__ h0,
-             __nv_bfloat16* __restrict__ o, float* __restrict__ hT, int T, int H,
-             int nchunks) {
+    gdn_scan(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+             const __grid_constant__ CUtensorMap tm_wk, const __grid_constant__ CUtensorMap tm_u,
+             const __grid_constant__ CUtensorMap tm_qk, const __nv_bfloat16* __restrict__ ws,
+             const float* __restrict__ h0, __nv_bfloat16* __restrict__ o, float* __restrict__ hT,
+             int T, int H, int nchunks, int* err) {
   using L = ScanSmem<DK>;
   using W = Ws<DK, DV>;
-  extern __shared__ __align__(16) uint8_t sm[];
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const uint32_t sb = saddr(sm);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   constexpr int kSlices = DV / kSlice;
   const int slice = blockIdx.x % kSlices;
@@ -423,42 +480,40 @@ __global__ void __launch_bounds__(256, 1)
   const int b = bh / H, h = bh - (bh / H) * H;
   const int v0 = slice * kSlice;
   const int g8 = lane >> 2, t2 = (lane & 3) * 2;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + L::kBar);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + L::kBar + 16);
 
-  auto stage_ptr = [&](int s, int off) { return sm + s * L::kStage + off; };
-  auto prefetch = [&](int s, int chunk) {
+  auto issue = [&](int s, int chunk) {  // thread 0 only
     const int t0 = chunk * kC;
-    const __nv_bfloat16* wsc = ws + (static_cast<int64_t>(bh) * nchunks + chunk) * (W::kBytes / 2);
-    __nv_bfloat16* Qs = reinterpret_cast<__nv_bfloat16*>(stage_ptr(s, L::kQs));
-    __nv_bfloat16* Ks = reinterpret_cast<__nv_bfloat16*>(stage_ptr(s, L::kKs));
-    __nv_bfloat16* Wks = reinterpret_cast<__nv_bfloat16*>(stage_ptr(s, L::kWks));
-    __nv_bfloat16* Us = reinterpret_cast<__nv_bfloat16*>(stage_ptr(s, L::kUs));
-    __nv_bfloat16* QKs = reinterpret_cast<__nv_bfloat16*>(stage_ptr(s, L::kQKs));
-    float* egs = reinterpret_cast<float*>(stage_ptr(s, L::kEg));
-    constexpr int kPkK = DK / 8;
-    for (int i = tid; i < kC * kPkK; i += 256) {
-      const int r = i / kPkK, c = (i - r * kPkK) * 8;
-      const int t = t0 + r;
-      const bool ok = t < T;
-      const int64_t off = ((static_cast<int64_t>(b) * T + (ok ? t : 0)) * H + h) * DK + c;
-      cp_async16_zfill(Qs + r * L::kLdK + c, q + off, ok);
-      cp_async16_zfill(Ks + r * L::kLdK + c, k + off, ok);
-      cp_async16(Wks + r * L::kLdK + c, wsc + W::kWk + r * DK + c);
+    const int unit = bh * nchunks + chunk;  // workspace chunk index
+    uint8_t* st = sm + s * L::kStage;
+    sm100::mbar_arrive_expect_tx(&full[s], L::kLoadBytes);
+#pragma unroll
+    for (int c = 0; c < DK / 64; ++c) {
+      sm100::tma_load_4d(st + L::kQs + c * 8192, &tm_q, &full[s], c * 64, h, t0, b);
+      sm100::tma_load_4d(st + L::kKs + c * 8192, &tm_k, &full[s], c * 64, h, t0, b);
+      sm100::tma_load_3d(st + L::kWks + c * 8192, &tm_wk, &full[s], c * 64, 0, unit);
     }
-    for (int i = tid; i < kC * (kSlice / 8); i += 256) {
-      const int r = i >> 3, c = (i & 7) * 8;
-      cp_async16(Us + r * L::kLdS + c, wsc + W::kU + r * DV + v0 + c);
-      cp_async16(QKs + r * L::kLdS + c, wsc + W::kQK + r * kC + c);
-    }
-    if (tid < W::kTailFloats / 4)
-      cp_async16(egs + tid * 4, reinterpret_cast<const float*>(wsc) + W::kQsc + tid * 4);
+    sm100::tma_load_3d(st + L::kUs, &tm_u, &full[s], v0, 0, unit);
+    sm100::tma_load_3d(st + L::kQKs, &tm_qk, &full[s], 0, 0, unit);
+    sm100::bulk_load(st + L::kEg,
+                     reinterpret_cast<const float*>(ws + static_cast<int64_t>(unit) * (W::kBytes / 2)) +
+                         W::kQsc,
+                     L::kTailBytes, &full[s]);
   };
 
   __nv_bfloat16* Ss = reinterpret_cast<__nv_bfloat16*>(sm + L::kSs);
   __nv_bfloat16* Es = reinterpret_cast<__nv_bfloat16*>(sm + L::kEs);
   __nv_bfloat16* Ed = reinterpret_cast<__nv_bfloat16*>(sm + L::kEd);
 
-  prefetch(0, 0);
-  cp_commit();
+  if (tid == 0) {
+    sm100::mbar_init(&full[0], 1);
+    sm100::mbar_init(&full[1], 1);
+    *abort_flag = 0;
+    sm100::fence_mbar_init();
+  }
+  __syncthreads();
+  if (tid == 0) issue(0, 0);
 
   // State: warp w owns rows 16w..16w+15 of S (DK = 128: rows 0..127) as
   // 8 n-tiles of 16 x 8 accumulators (the 64-column slice).
@@ -490,19 +545,22 @@ __global__ void __launch_bounds__(256, 1)
 
   // Output tiles: warp w -> rows 16(w%4).., columns 32(w/4).. of the 64 x 64 o slice.
   const int om0 = (warp & 3) * 16, on0 = (warp >> 2) * 32;
+  int failed_at = -1;
 
   for (int chunk = 0; chunk < nchunks; ++chunk) {
     const int s = chunk & 1;
-    if (chunk + 1 < nchunks) prefetch(s ^ 1, chunk + 1);
-    cp_commit();
-    cp_wait<1>();
-    __syncthreads();  // chunk's data and the published state are visible
-    const __nv_bfloat16* Qs = reinterpret_cast<const __nv_bfloat16*>(stage_ptr(s, L::kQs));
-    const __nv_bfloat16* Ks = reinterpret_cast<const __nv_bfloat16*>(stage_ptr(s, L::kKs));
-    const __nv_bfloat16* Wks = reinterpret_cast<const __nv_bfloat16*>(stage_ptr(s, L::kWks));
-    const __nv_bfloat16* Us = reinterpret_cast<const __nv_bfloat16*>(stage_ptr(s, L::kUs));
-    const __nv_bfloat16* QKs = reinterpret_cast<const __nv_bfloat16*>(stage_ptr(s, L::kQKs));
-    const float* egs = reinterpret_cast<const float*>(stage_ptr(s, L::kEg));
+    // Stage s^1 was released by the barrier that ended the previous chunk.
+    if (tid == 0 && chunk + 1 < nchunks) issue(s ^ 1, chunk + 1);
+    const bool landed = sm100::mbar_wait(&full[s], (chunk >> 1) & 1, err, abort_flag);
+    if (!__syncthreads_and(landed)) {  // also: the published state is visible
+      failed_at = chunk;
+      break;
+    }
+    const uint32_t st = sb + s * L::kStage;
+    const uint32_t sQ = st + L::kQs, sK = st + L::kKs, sW = st + L::kWks;
+    const uint32_t sU = st + L::kUs, sQK = st + L::kQKs;
+    const uint8_t* Ub = sm + s * L::kStage + L::kUs;
+    const float* egs = reinterpret_cast<const float*>(sm + s * L::kStage + L::kEg);
     const float* qsc = egs;            // scale * exp(gc_l)
     const float* dcy = egs + kC;       // exp(gc_last - gc_l)
     const float egl = egs[2 * kC];     // exp(gc_last)
@@ -515,8 +573,8 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll
     for (int kk = 0; kk < DK / 16; ++kk) {
       uint32_t aw[4], aq[4];
-      frag_a(aw, Wks, L::kLdK, om0, kk * 16);
-      frag_a(aq, Qs, L::kLdK, om0, kk * 16);
+      sfrag_a(aw, sW, om0, kk * 16);
+      sfrag_a(aq, sQ, om0, kk * 16);
 #pragma unroll
       for (int n = 0; n < 4; n += 2) {
         uint32_t bb[4];
@@ -533,7 +591,8 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         const int l = om0 + g8 + half * 8, c = on0 + n * 8 + t2;
-        const __nv_bfloat162 u2 = *reinterpret_cast<const __nv_bfloat162*>(Us + l * L::kLdS + c);
+        const __nv_bfloat162 u2 =
+            *reinterpret_cast<const __nv_bfloat162*>(Ub + swz(l, c - t2) + t2 * 2);
         const float e0 = __bfloat162float(u2.x) - ws_acc[n][half * 2];
         const float e1 = __bfloat162float(u2.y) - ws_acc[n][half * 2 + 1];
         const float dec = dcy[l];
@@ -547,7 +606,7 @@ __global__ void __launch_bounds__(256, 1)
     // o += QKm err  (QKm lower triangular: k-blocks 0 .. this warp's row block)
     for (int kk = 0; kk <= (warp & 3); ++kk) {
       uint32_t a[4];
-      frag_a(a, QKs, L::kLdS, om0, kk * 16);
+      sfrag_a(a, sQK, om0, kk * 16);
 #pragma unroll
       for (int n = 0; n < 4; n += 2) {
         uint32_t bb[4];
@@ -579,7 +638,7 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll
       for (int kk = 0; kk < kC / 16; ++kk) {
         uint32_t a[4];
-        frag_a_t(a, Ks, L::kLdK, sr0, kk * 16);
+        sfrag_a_t(a, sK, sr0, kk * 16);
 #pragma unroll
         for (int n = 0; n < 8; n += 2) {
           uint32_t bb[4];
@@ -592,7 +651,15 @@ __global__ void __launch_bounds__(256, 1)
     __syncthreads();  // Es / Ed and this stage are free; Ss may be rewritten
     publish_state();
   }
-  cp_wait<0>();
+  if (failed_at >= 0) {
+    // A wait gave up: let the copies already issued (this chunk's and the
+    // next one's) land before leaving.
+    if (tid == 0)
+      for (int c = failed_at; c < failed_at + 2 && c < nchunks; ++c)
+        sm100::mbar_wait(&full[c & 1], (c >> 1) & 1, nullptr, abort_flag, true);
+    __syncthreads();
+    return;
+  }
   if (owns_rows && hT) {
 #pragma unroll
     for (int n = 0; n < 8; ++n)
@@ -611,8 +678,27 @@ int launch_gdn(const void* q, const void* k, const void* v, const float* g, cons
   const int nchunks = (T + kC - 1) / kC;
   auto k1 = gdn_prepare<DK, DV>;
   auto k2 = gdn_scan<DK, DV>;
-  const int smem1 = PrepSmem<DK, DV>::kBytes;
-  const int smem2 = ScanSmem<DK>::kBytes;
+  CUtensorMap tq, tk, tv;
+  if (!make_bshd_map(&tq, q, DK, H, T, B, kC, true) || !make_bshd_map(&tk, k, DK, H, T, B, kC, true) ||
+      !make_bshd_map(&tv, v, DV, H, T, B, kC, true))
+    return TILEOPS_ELAUNCH;
+  const int smem1 = PrepSmem<DK, DV>::kAlloc;
+  const int smem2 = ScanSmem<DK>::kAlloc;
+  // Workspace tiles as 3-D maps (columns, 64 rows, chunk units).
+  const uint64_t units = static_cast<uint64_t>(B) * H * nchunks;
+  const uint64_t wb = Ws<DK, DV>::kBytes;
+  CUtensorMap twk, tu, tqk;
+  {
+    auto* base = static_cast<const uint8_t*>(ws);
+    const uint64_t dk_dims[3] = {DK, kC, units}, dk_str[2] = {DK * 2, wb};
+    const uint64_t dv_dims[3] = {DV, kC, units}, dv_str[2] = {DV * 2, wb};
+    const uint64_t c_dims[3] = {kC, kC, units}, c_str[2] = {kC * 2, wb};
+    const uint32_t box[3] = {64, kC, 1};
+    if (!make_tiled_map_16bit(&twk, base + Ws<DK, DV>::kWk * 2, true, 3, dk_dims, dk_str, box) ||
+        !make_tiled_map_16bit(&tu, base + Ws<DK, DV>::kU * 2, true, 3, dv_dims, dv_str, box) ||
+        !make_tiled_map_16bit(&tqk, base + Ws<DK, DV>::kQK * 2, true, 3, c_dims, c_str, box))
+      return TILEOPS_ELAUNCH;
+  }
   if (cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, smem1) !=
           cudaSuccess ||
       cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, smem2) != cudaSuccess)
@@ -620,15 +706,13 @@ int launch_gdn(const void* q, const void* k, const void* v, const float* g, cons
   const int64_t grid1 = static_cast<int64_t>(B) * H * nchunks;
   if (grid1 > 0x7fffffffLL) return TILEOPS_EBADSHAPE;
   k1<<<static_cast<unsigned>(grid1), 128, smem1, s>>>(
-      static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
-      static_cast<const __nv_bfloat16*>(v), g, beta, static_cast<__nv_bfloat16*>(ws), T, H,
-      nchunks, scale);
+      tq, tk, tv, g, beta, static_cast<__nv_bfloat16*>(ws), T, H, nchunks, scale,
+      device_error_ptr());
   int st = launch_status();
   if (st != TILEOPS_OK) return st;
   k2<<<static_cast<unsigned>(B * H * (DV / kSlice)), 256, smem2, s>>>(
-      static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
-      static_cast<const __nv_bfloat16*>(ws), h0, static_cast<__nv_bfloat16*>(o), hT, T, H,
-      nchunks);
+      tq, tk, twk, tu, tqk, static_cast<const __nv_bfloat16*>(ws), h0,
+      static_cast<__nv_bfloat16*>(o), hT, T, H, nchunks, device_error_ptr());
   return launch_status();
 }
 
