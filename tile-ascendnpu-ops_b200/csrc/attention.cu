@@ -31,7 +31,9 @@
 // warps may then rescale O_t in TMEM and overwrite S_t with P_t.
 // Softmax: the running max moves (and O is rescaled) only when it grows by
 // more than 8 in log2 units, so P <= 256 and rescales are rare; exp2 is
-// ex2.approx on exp2(scale*log2e*s - m) (one FFMA + one MUFU per score).
+// ex2.approx on exp2(scale*log2e*s - m), the FMA and the row sum as packed
+// f32x2 instructions; each pass over S keeps the next 32-column TMEM load in
+// flight while the current one is processed.
 // Every mbarrier wait is bounded (2 s): on timeout the kernel records an
 // error (tileops_device_error_flag), drains its copies / MMAs, frees TMEM and
 // returns.
@@ -87,6 +89,26 @@ struct Params {
   float* lse;
   int* err;
 };
+
+// Packed fp32x2 FMA / add (sm_100a): one instruction for two lanes of work.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
 
 __device__ __forceinline__ uint32_t pack2(float a, float b, bool bf16) {
   if (bf16) {
@@ -275,23 +297,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool need_mask = (k0 + kBN > p.seq_kv) || (p.causal && k0 + kBN - 1 > q0 + off);
       // Keys this row may see in the block: [k0, k0 + nvis).
       const int nvis = need_mask ? max(0, min(kBN, min(p.seq_kv - 1, row_limit) + 1 - k0)) : kBN;
-      // Pass 1: row max of the raw scores (scale > 0 commutes with max),
-      // 8 independent accumulators.
+      // Pass 1: row max of the raw scores (scale > 0 commutes with max), 8
+      // chains; the TMEM load of 32-column chunk c+1 is in flight while chunk
+      // c is reduced.
       float mx[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) mx[i] = -INFINITY;
+      {
+        uint32_t ra[32], rb[32];
+        tmem_ld32(t_s, ra);
+        tmem_wait_ld_regs(ra);
 #pragma unroll
-      for (int c = 0; c < kBN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(t_s + c * 32, r);
-        tmem_wait_ld();
-        if (!need_mask) {
+        for (int c = 0; c < kBN / 32; ++c) {
+          uint32_t(&cur)[32] = (c & 1) ? rb : ra;
+          uint32_t(&nxt)[32] = (c & 1) ? ra : rb;
+          if (c + 1 < kBN / 32) tmem_ld32(t_s + (c + 1) * 32, nxt);
+          if (!need_mask) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) mx[i & 7] = fmaxf(mx[i & 7], __uint_as_float(r[i]));
-        } else {
+            for (int i = 0; i < 32; ++i) mx[i & 7] = fmaxf(mx[i & 7], __uint_as_float(cur[i]));
+          } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (c * 32 + i < nvis) mx[i & 7] = fmaxf(mx[i & 7], __uint_as_float(r[i]));
+            for (int i = 0; i < 32; ++i)
+              if (c * 32 + i < nvis) mx[i & 7] = fmaxf(mx[i & 7], __uint_as_float(cur[i]));
+          }
+          if (c + 1 < kBN / 32) tmem_wait_ld_regs(nxt);
         }
       }
       const float mraw = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
@@ -307,7 +336,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < D / 32; ++c) {
           uint32_t r[32];
           tmem_ld32(t_o + c * 32, r);
-          tmem_wait_ld();
+          tmem_wait_ld_regs(r);
 #pragma unroll
           for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
           tmem_st32(t_o + c * 32, r);
@@ -315,38 +344,41 @@ __global__ void __launch_bounds__(kThreads, 1)
         l *= alpha;
       }
       m = m_use;
-      // Pass 2: P = exp2(scale*log2e*s - m), packed to 16-bit pairs over S,
-      // 4 independent partial sums.
-      float ps[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      // Pass 2: P = exp2(scale*log2e*s - m) two scores at a time (packed
+      // f32x2 FMA and add), packed to 16-bit pairs over S columns already
+      // read; chunk c+1's TMEM load overlaps chunk c's exponentials.
+      float2 ps[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
+      {
+        const float2 scale2 = make_float2(sl2, sl2), negm2 = make_float2(-m_sub, -m_sub);
+        uint32_t ra[32], rb[32];
+        tmem_ld32(t_s, ra);
+        tmem_wait_ld_regs(ra);
 #pragma unroll
-      for (int c = 0; c < kBN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(t_s + c * 32, r);
-        tmem_wait_ld();
-        uint32_t pk[16];
-        if (!need_mask) {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float e0 = ex2(fmaf(__uint_as_float(r[2 * i]), sl2, -m_sub));
-            const float e1 = ex2(fmaf(__uint_as_float(r[2 * i + 1]), sl2, -m_sub));
-            ps[i & 3] += e0 + e1;
-            pk[i] = pack2(e0, e1, BF16);
-          }
-        } else {
+        for (int c = 0; c < kBN / 32; ++c) {
+          uint32_t(&cur)[32] = (c & 1) ? rb : ra;
+          uint32_t(&nxt)[32] = (c & 1) ? ra : rb;
+          if (c + 1 < kBN / 32) tmem_ld32(t_s + (c + 1) * 32, nxt);
+          uint32_t pk[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const int kk = c * 32 + 2 * i;
-            const float e0 = kk < nvis ? ex2(fmaf(__uint_as_float(r[2 * i]), sl2, -m_sub)) : 0.0f;
-            const float e1 =
-                kk + 1 < nvis ? ex2(fmaf(__uint_as_float(r[2 * i + 1]), sl2, -m_sub)) : 0.0f;
-            ps[i & 3] += e0 + e1;
+            const float2 x = ffma2(
+                make_float2(__uint_as_float(cur[2 * i]), __uint_as_float(cur[2 * i + 1])), scale2,
+                negm2);
+            float e0 = ex2(x.x), e1 = ex2(x.y);
+            if (need_mask) {
+              e0 = kk < nvis ? e0 : 0.0f;
+              e1 = kk + 1 < nvis ? e1 : 0.0f;
+            }
+            ps[i & 1] = fadd2(ps[i & 1], make_float2(e0, e1));
             pk[i] = pack2(e0, e1, BF16);
           }
+          // P columns [16c, 16c+16) lie in S columns already read.
+          tmem_st16(t_s + c * 16, pk);
+          if (c + 1 < kBN / 32) tmem_wait_ld_regs(nxt);
         }
-        // P columns [16c, 16c+16) lie in S columns already read.
-        tmem_st16(t_s + c * 16, pk);
       }
-      const float rowsum = (ps[0] + ps[1]) + (ps[2] + ps[3]);
+      const float rowsum = (ps[0].x + ps[1].x) + (ps[0].y + ps[1].y);
       l += rowsum;
       tmem_wait_st();
       tc_fence_before();
@@ -363,7 +395,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < D / 32; ++c) {
         uint32_t r[32];
         tmem_ld32(t_o + c * 32, r);
-        tmem_wait_ld();
+        tmem_wait_ld_regs(r);
         if (q_idx < p.seq_q) {
 #pragma unroll
           for (int u = 0; u < 4; ++u) {

@@ -69,6 +69,14 @@ struct Cvt<__nv_bfloat16> {
 // Streaming loads bypass L1 allocation (each byte is touched once); stores
 // use the evict-first (.cs) hint so the output stream does not displace
 // inputs still needed by other CTAs from L2.
+// An empty volatile asm that claims to rewrite v: placed after a group of
+// ld_stream calls, it keeps the compiler from hoisting any use of v (and so
+// any arithmetic on it) above the last load of the group, so every load of
+// the group is in flight before the first result is consumed.
+__device__ __forceinline__ void after_loads(uint4& v) {
+  asm volatile("" : "+r"(v.x), "+r"(v.y), "+r"(v.z), "+r"(v.w));
+}
+
 __device__ __forceinline__ uint4 ld_stream(const void* p) {
   uint4 r;
   asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
@@ -101,6 +109,43 @@ union Pack16 {
 
 // Grid for a grid-stride streaming loop: enough CTAs to cover `work` items
 // of `per_cta` each, capped at `waves` full waves over the SMs.
+// Division of 32-bit unsigned numerators by a divisor fixed at launch, as a
+// multiply-high, an add and a shift (Granlund & Montgomery, "Division by
+// invariant integers using multiplication", PLDI 1994): with
+// s = ceil(log2 d) and m = floor(2^32 (2^s - d) / d) + 1,
+// n / d = (umulhi(n, m) + n) >> s for every n < 2^32.
+struct FastDivU32 {
+  uint32_t d, m, s;
+  explicit FastDivU32(uint32_t divisor = 1) : d(divisor), m(0), s(0) {
+    while ((1ull << s) < d) ++s;
+    m = static_cast<uint32_t>((((1ull << s) - d) << 32) / d + 1);
+  }
+  __device__ __forceinline__ uint32_t div(uint32_t n) const {
+    return static_cast<uint32_t>(
+        (static_cast<uint64_t>(__umulhi(n, m)) + n) >> s);
+  }
+};
+
+// CTAs of `kernel` that fit on one SM at `threads` threads per CTA (at least 1).
+template <typename Kernel>
+int resident_ctas(Kernel kernel, int threads, size_t smem = 0) {
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, smem) != cudaSuccess ||
+      n < 1)
+    n = 1;
+  return n;
+}
+
+// Grid of a grid-stride streaming kernel: enough CTAs for the work, at most
+// one full wave (every SM holding `resident` CTAs), so no CTA waits for a
+// second wave while others run.
+inline unsigned stream_grid_resident(int64_t work, int64_t per_cta, int resident) {
+  int64_t need = (work + per_cta - 1) / per_cta;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * resident;
+  if (need < 1) need = 1;
+  return static_cast<unsigned>(need < cap ? need : cap);
+}
+
 inline unsigned stream_grid(int64_t work, int64_t per_cta, int waves) {
   int64_t need = (work + per_cta - 1) / per_cta;
   int64_t cap = static_cast<int64_t>(sm_count()) * waves;

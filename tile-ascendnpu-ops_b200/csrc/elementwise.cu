@@ -121,7 +121,9 @@ int launch_map_t(const void* x, void* y, int64_t n, F f, cudaStream_t s) {
   T* yp = static_cast<T*>(y);
   if (aligned16(x) && aligned16(y)) {
     constexpr int V = 16 / sizeof(T);
-    const unsigned grid = stream_grid(n / V + 1, static_cast<int64_t>(kThreads) * kUnroll, 8);
+    static const int res = resident_ctas(unary_map_vec<T, F>, kThreads);
+    const unsigned grid =
+        stream_grid_resident(n / V + 1, static_cast<int64_t>(kThreads) * kUnroll, res);
     unary_map_vec<T, F><<<grid, kThreads, 0, s>>>(xp, yp, n, f);
   } else {
     const unsigned grid = stream_grid(n, kThreads, 8);
@@ -238,7 +240,8 @@ int launch_pred_t(const void* x, void* y, int64_t n, cudaStream_t s) {
   const T* xp = static_cast<const T*>(x);
   uint8_t* yp = static_cast<uint8_t*>(y);
   if (aligned16(x) && aligned16(y)) {
-    const unsigned grid = stream_grid(n / 16 + 1, kThreads * 2, 8);
+    static const int res = resident_ctas(predicate_vec<T, P>, kThreads);
+    const unsigned grid = stream_grid_resident(n / 16 + 1, kThreads * 2, res);
     predicate_vec<T, P><<<grid, kThreads, 0, s>>>(xp, yp, n);
   } else {
     predicate_scalar<T, P><<<stream_grid(n, kThreads, 8), kThreads, 0, s>>>(xp, yp, n);
@@ -361,7 +364,8 @@ extern "C" int tileops_bitwise_not_fwd(const void* x, void* y, int64_t n, int dt
   const uint8_t* xp = static_cast<const uint8_t*>(x);
   uint8_t* yp = static_cast<uint8_t*>(y);
   if (aligned16(x) && aligned16(y)) {
-    const unsigned grid = stream_grid(nbytes / 16 + 1, kThreads * kUnroll, 8);
+    static const int res = resident_ctas(xor_stream_vec, kThreads);
+    const unsigned grid = stream_grid_resident(nbytes / 16 + 1, kThreads * kUnroll, res);
     xor_stream_vec<<<grid, kThreads, 0, s>>>(xp, yp, nbytes, mask);
   } else {
     xor_stream_scalar<<<stream_grid(nbytes, kThreads, 8), kThreads, 0, s>>>(

@@ -77,7 +77,7 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
 // Workspace of one chunk (element offsets into a bf16 array, then fp32 tail).
 template <int DK, int DV>
 struct Ws {
-  static constexpr int64_t kWk = 0;                 // C x DK bf16
+  static constexpr int64_t kWk = 0;                 // C x DK bf16, holds -Wk
   static constexpr int64_t kU = kWk + kC * DK;      // C x DV bf16
   static constexpr int64_t kQK = kU + kC * DV;      // C x C bf16
   static constexpr int64_t kHalfs = kQK + kC * kC;  // bf16 elements before the fp32 tail
@@ -419,11 +419,15 @@ __global__ void __launch_bounds__(128, 3)
             mma_bf16(acc[n + 1], a, bb[2], bb[3]);
           }
         }
+        // The workspace keeps -Wk (the scans add it) and U.
+        const float sg = which == 0 ? -1.0f : 1.0f;
 #pragma unroll
         for (int n = 0; n < 8; ++n) {
           const int l = m0 + g8, c = n0 + n * 8 + t2;
-          *reinterpret_cast<uint32_t*>(out + l * D + c) = pack_bf16(acc[n][0], acc[n][1]);
-          *reinterpret_cast<uint32_t*>(out + (l + 8) * D + c) = pack_bf16(acc[n][2], acc[n][3]);
+          *reinterpret_cast<uint32_t*>(out + l * D + c) =
+              pack_bf16(sg * acc[n][0], sg * acc[n][1]);
+          *reinterpret_cast<uint32_t*>(out + (l + 8) * D + c) =
+              pack_bf16(sg * acc[n][2], sg * acc[n][3]);
         }
       }
     }
@@ -564,7 +568,7 @@ __global__ void __launch_bounds__(256, 1)
     const float* qsc = egs;            // scale * exp(gc_l)
     const float* dcy = egs + kC;       // exp(gc_last - gc_l)
     const float egl = egs[2 * kC];     // exp(gc_last)
-    // err = U - Wk S ; qs = Q S   (this warp's 16 x 32 tile)
+    // err = U - Wk S (the workspace holds -Wk) ; qs = Q S   (this warp's 16 x 32 tile)
     float ws_acc[4][4], qs_acc[4][4];
 #pragma unroll
     for (int n = 0; n < 4; ++n)
@@ -593,8 +597,8 @@ __global__ void __launch_bounds__(256, 1)
         const int l = om0 + g8 + half * 8, c = on0 + n * 8 + t2;
         const __nv_bfloat162 u2 =
             *reinterpret_cast<const __nv_bfloat162*>(Ub + swz(l, c - t2) + t2 * 2);
-        const float e0 = __bfloat162float(u2.x) - ws_acc[n][half * 2];
-        const float e1 = __bfloat162float(u2.y) - ws_acc[n][half * 2 + 1];
+        const float e0 = __bfloat162float(u2.x) + ws_acc[n][half * 2];  // U + (-Wk) S
+        const float e1 = __bfloat162float(u2.y) + ws_acc[n][half * 2 + 1];
         const float dec = dcy[l];
         *reinterpret_cast<uint32_t*>(Es + l * L::kLdS + c) = pack_bf16(e0, e1);
         *reinterpret_cast<uint32_t*>(Ed + l * L::kLdS + c) = pack_bf16(dec * e0, dec * e1);
@@ -671,6 +675,345 @@ __global__ void __launch_bounds__(256, 1)
   }
 }
 
+// =========================================================== kernel 2b
+// gdn_scan_tc: the chunk scan on the 5th-generation tensor cores (dk = 128).
+// One CTA per (b, h, 64-column slice of dv), 320 threads:
+//   warps 0-7  math: warp w serves TMEM lanes 32 (w % 4).. (rows of every
+//              accumulator) and columns 32 (w / 4).. of the 64-wide slice
+//   warp 8     TMA producer (two stages, one chunk ahead)
+//   warp 9     MMA issuer (one thread) and TMEM owner (512 columns)
+// TMEM: D1 x3 [128 x 64] at columns 0 / 64 / 128, D2 x2 at 192 / 256, the
+// state S [128 x 64] at 320.
+// Per chunk c (S the state at the chunk start, Sb its bf16 copy in smem; the
+// workspace holds -Wk):
+//   MMA0  D1 = [I ; 0] U            (no dependence on S: issued early)
+//   MMA1  D1 += [-Wk ; Q] Sb        (rows 0-63: err = U - Wk S, 64-127: Q S)
+//   math  Es = err, Ed = e^(gc_last - gc) err (bf16)           (rows 0-63)
+//   MMA3  S += K^T Ed               (S pre-scaled by e^gc_last), commit
+//   MMA2  D2 = [U ; QKm] Es         (rows 64-127: QKm err)
+//   math  S -> Sb (bf16), S *= e^(gc_last of chunk c+1)   -> next chunk
+//   math  o = scale e^gc (Q S) + QKm err   (rows 64-127, off the chain)
+// The chain from one chunk to the next is MMA1, the err pass, MMA3 and the
+// state pass; D1 is triple- and D2 double-buffered so the output pass of
+// chunk c overlaps chunk c+1.
+// Shared memory per stage (128-byte swizzled tiles, 64 KB): A1 = [-Wk ; Q]
+// as two chunks of [128][64]; K [64][128]; [U ; QKm] as one [128][64] tile
+// (the B operand of MMA0 is its U half; as the A operand of MMA2 its U rows
+// only feed rows of D2 that are never read).  Outside the stages: the
+// identity tile [I ; 0], the fp32 tails, Sb [128][64] (MN-major B of MMA1),
+// Es, Ed [64][64] (MN-major B of MMA2 / MMA3).
+constexpr int kTcStages = 2;
+struct ScanTcSmem {
+  static constexpr int kA1 = 0;                           // 2 x 16 KB
+  static constexpr int kK = kA1 + 2 * 16384;              // 2 x 8 KB
+  static constexpr int kUQ = kK + 2 * 8192;               // U 8 KB, then QKm 8 KB
+  static constexpr int kStage = kUQ + 16384;              // 64 KB
+  static constexpr int kTailBytes = (2 * kC + 4) * 4;
+  static constexpr int kLoadBytes = 2 * 8192 /*Wk*/ + 2 * 8192 /*Q*/ + 2 * 8192 /*K*/ +
+                                    8192 /*U*/ + 8192 /*QKm*/ + kTailBytes;
+  static constexpr int kId = kTcStages * kStage;          // 16 KB
+  static constexpr int kSb = kId + 16384;                 // 16 KB
+  static constexpr int kEs = kSb + 16384;                 // 8 KB
+  static constexpr int kEd = kEs + 8192;                  // 8 KB
+  static constexpr int kTail = kEd + 8192;                // kTcStages x 528 B
+  static constexpr int kBar = kTail + kTcStages * kTailBytes;
+  static constexpr int kBytes = kBar + 128;
+  static constexpr int kAlloc = kBytes + 1024;
+  static_assert(kAlloc <= 232448, "scan_tc shared memory exceeds 227 KB");
+};
+
+struct ScanTcBars {
+  uint64_t full[kTcStages], empty[kTcStages];
+  uint64_t s_ready, d1_full, e_ready, d3_full, d2_full, drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+constexpr int kScanTcMath = 256;
+constexpr int kScanTcThreads = kScanTcMath + 64;
+constexpr uint32_t kScanTcCols = 512;
+
+template <int DV>
+__global__ void __launch_bounds__(kScanTcThreads, 1)
+    gdn_scan_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                const __grid_constant__ CUtensorMap tm_wk,
+                const __grid_constant__ CUtensorMap tm_u,
+                const __grid_constant__ CUtensorMap tm_qk, const __nv_bfloat16* __restrict__ ws,
+                const float* __restrict__ h0, __nv_bfloat16* __restrict__ o,
+                float* __restrict__ hT, int T, int H, int nchunks, int* err) {
+  using namespace sm100;
+  using L = ScanTcSmem;
+  using W = Ws<128, DV>;
+  constexpr int DK = 128;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  ScanTcBars* bars = reinterpret_cast<ScanTcBars*>(sm + L::kBar);
+  volatile int* abort_flag = &bars->abort_flag;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  constexpr int kSlices = DV / kSlice;
+  const int slice = blockIdx.x % kSlices;
+  const int bh = blockIdx.x / kSlices;
+  const int b = bh / H, h = bh - (bh / H) * H;
+  const int v0 = slice * kSlice;
+
+  if (tid == 0) {
+    for (int s = 0; s < kTcStages; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 1);
+    }
+    mbar_init(&bars->s_ready, kScanTcMath);
+    mbar_init(&bars->d1_full, 1);
+    mbar_init(&bars->e_ready, kScanTcMath);
+    mbar_init(&bars->d3_full, 1);
+    mbar_init(&bars->d2_full, 1);
+    mbar_init(&bars->drain, 1);
+    bars->abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(&bars->tmem_base, kScanTcCols);
+    tmem_relinquish();
+  }
+  if (tid < kScanTcMath) {
+    // The identity tile [I ; 0]: 128 rows x 64 bf16, K-major, swizzled.
+    for (int i = tid; i < 128 * 8; i += kScanTcMath) {
+      const int r = i >> 3, u = i & 7;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (r < 64 && (r >> 3) == u) {
+        uint32_t* vw = reinterpret_cast<uint32_t*>(&v);
+        vw[(r & 7) >> 1] = (r & 1) ? 0x3F800000u : 0x00003F80u;  // bf16 1.0 at column r
+      }
+      *reinterpret_cast<uint4*>(sm + L::kId + swz(r, 8 * u)) = v;
+    }
+    fence_proxy_async_smem();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+  const uint32_t t_s = tmem + 320;
+  auto t_d1 = [&](int c) { return tmem + 64u * static_cast<uint32_t>(c % 3); };
+  auto t_d2 = [&](int c) { return tmem + 192u + 64u * static_cast<uint32_t>(c & 1); };
+
+  if (warp == 8) {
+    // ------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      prefetch_tensormap(&tm_q);
+      prefetch_tensormap(&tm_k);
+      prefetch_tensormap(&tm_wk);
+      prefetch_tensormap(&tm_u);
+      prefetch_tensormap(&tm_qk);
+      int armed = -1;
+      for (int c = 0; c < nchunks; ++c) {
+        const int s = c % kTcStages;
+        const int use = c / kTcStages;
+        if (use > 0 && !mbar_wait(&bars->empty[s], (use - 1) & 1, err, abort_flag)) break;
+        uint8_t* st = sm + s * L::kStage;
+        const int t0 = c * kC;
+        const int unit = bh * nchunks + c;
+        mbar_arrive_expect_tx(&bars->full[s], L::kLoadBytes);
+#pragma unroll
+        for (int k = 0; k < DK / 64; ++k) {
+          tma_load_3d(st + L::kA1 + k * 16384, &tm_wk, &bars->full[s], k * 64, 0, unit);
+          tma_load_4d(st + L::kA1 + k * 16384 + 8192, &tm_q, &bars->full[s], k * 64, h, t0, b);
+          tma_load_4d(st + L::kK + k * 8192, &tm_k, &bars->full[s], k * 64, h, t0, b);
+        }
+        tma_load_3d(st + L::kUQ, &tm_u, &bars->full[s], v0, 0, unit);
+        tma_load_3d(st + L::kUQ + 8192, &tm_qk, &bars->full[s], 0, 0, unit);
+        bulk_load(sm + L::kTail + s * L::kTailBytes,
+                  reinterpret_cast<const float*>(ws + static_cast<int64_t>(unit) * (W::kBytes / 2)) +
+                      W::kQsc,
+                  L::kTailBytes, &bars->full[s]);
+        armed = c;
+      }
+      // Never leave with a bulk copy still writing this CTA's shared memory.
+      for (int c = armed - (kTcStages - 1); c <= armed; ++c)
+        if (c >= 0)
+          mbar_wait(&bars->full[c % kTcStages], (c / kTcStages) & 1, err, abort_flag, true);
+    }
+  } else if (warp == 9) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t id_kmn = idesc_f16_major(128, 64, 1, 0, 1);  // A K-major, B MN-major
+      constexpr uint32_t id_mnmn = idesc_f16_major(128, 64, 1, 1, 1);  // A MN-major (K^T)
+      const uint32_t id_base = smem_u32(sm + L::kId);
+      const uint32_t sb_base = smem_u32(sm + L::kSb);
+      const uint32_t es_base = smem_u32(sm + L::kEs);
+      const uint32_t ed_base = smem_u32(sm + L::kEd);
+      for (int c = 0; c < nchunks; ++c) {
+        const int s = c % kTcStages;
+        const uint32_t st = smem_u32(sm + s * L::kStage);
+        const uint32_t d1 = t_d1(c);
+        if (!mbar_wait(&bars->full[s], (c / kTcStages) & 1, err, abort_flag)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < kC / 16; ++kk)  // D1 = [I ; 0] U
+          mma_f16_ss(d1, smem_desc(id_base + kk * 32, 16, 1024),
+                     smem_desc(st + L::kUQ + kk * 2048, 8192, 1024), id_kmn, kk > 0);
+        if (!mbar_wait(&bars->s_ready, c & 1, err, abort_flag)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < DK / 16; ++kk)  // D1 += [-Wk ; Q] Sb
+          mma_f16_ss(d1,
+                     smem_desc(st + L::kA1 + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
+                     smem_desc(sb_base + kk * 2048, 16384, 1024), id_kmn, 1);
+        mma_commit(&bars->d1_full);
+        if (!mbar_wait(&bars->e_ready, c & 1, err, abort_flag)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < kC / 16; ++kk)  // S += K^T Ed
+          mma_f16_ss(t_s, smem_desc(st + L::kK + kk * 2048, 8192, 1024),
+                     smem_desc(ed_base + kk * 2048, 8192, 1024), id_mnmn, 1);
+        mma_commit(&bars->d3_full);
+#pragma unroll
+        for (int kk = 0; kk < kC / 16; ++kk)  // D2 = [U ; QKm] Es
+          mma_f16_ss(t_d2(c), smem_desc(st + L::kUQ + kk * 32, 16, 1024),
+                     smem_desc(es_base + kk * 2048, 8192, 1024), id_kmn, kk > 0);
+        mma_commit(&bars->d2_full);
+        mma_commit(&bars->empty[s]);
+      }
+      // Every MMA issued completes before TMEM is freed.
+      mma_commit(&bars->drain);
+      mbar_wait(&bars->drain, 0, err, abort_flag, true);
+    }
+  } else {
+    // ------------------------------------------------------- math warps 0-7
+    const int q = warp & 3;                 // TMEM lane quadrant
+    const int r = q * 32 + lane;            // accumulator row (state row / token row)
+    const int cb = (warp >> 2) * 32;        // first column of this warp's half
+    const int l = r & 63;                   // token of rows 0-63 / 64-127
+    const bool err_rows = q < 2;
+    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    uint8_t* Sb = sm + L::kSb;
+    uint8_t* Es = sm + L::kEs;
+    uint8_t* Ed = sm + L::kEd;
+    bool ok = true;
+    // This thread's 32 state values (fp32, row r, columns cb..cb+31) -> Sb in
+    // bf16; then, scaled by e^gc_last of chunk `next`, back to TMEM.
+    auto publish = [&](uint32_t (&x)[32], int next) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        uint4 pk;
+        pk.x = pack_bf16(__uint_as_float(x[8 * u + 0]), __uint_as_float(x[8 * u + 1]));
+        pk.y = pack_bf16(__uint_as_float(x[8 * u + 2]), __uint_as_float(x[8 * u + 3]));
+        pk.z = pack_bf16(__uint_as_float(x[8 * u + 4]), __uint_as_float(x[8 * u + 5]));
+        pk.w = pack_bf16(__uint_as_float(x[8 * u + 6]), __uint_as_float(x[8 * u + 7]));
+        *reinterpret_cast<uint4*>(Sb + swz(r, cb + 8 * u)) = pk;
+      }
+      fence_proxy_async_smem();
+      const int s = next % kTcStages;
+      if (!mbar_wait(&bars->full[s], (next / kTcStages) & 1, err, abort_flag)) {
+        ok = false;
+        return;
+      }
+      const float egl = reinterpret_cast<const float*>(sm + L::kTail + s * L::kTailBytes)[2 * kC];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) x[i] = __float_as_uint(__uint_as_float(x[i]) * egl);
+      tmem_st32(t_s + lane_off + cb, x);
+      tmem_wait_st();
+    };
+    {
+      uint32_t x[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        x[i] = __float_as_uint(
+            h0 ? h0[((static_cast<int64_t>(b) * H + h) * DK + r) * DV + v0 + cb + i] : 0.0f);
+      publish(x, 0);
+      tc_fence_before();
+      mbar_arrive(&bars->s_ready);
+    }
+    for (int c = 0; ok && c < nchunks; ++c) {
+      const int s = c % kTcStages;
+      const float* tail = reinterpret_cast<const float*>(sm + L::kTail + s * L::kTailBytes);
+      float qsc = 0.0f;
+      if (err_rows) {
+        // err = U - Wk S for token l (D1 rows 0-63) -> Es, Ed rows l.
+        if (!mbar_wait(&bars->d1_full, c & 1, err, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        uint32_t x[32];
+        tmem_ld32(t_d1(c) + lane_off + cb, x);
+        tmem_wait_ld_regs(x);
+        const float dec = tail[kC + l];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          uint4 pe, pd;
+          uint32_t* pew = reinterpret_cast<uint32_t*>(&pe);
+          uint32_t* pdw = reinterpret_cast<uint32_t*>(&pd);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float e0 = __uint_as_float(x[8 * u + 2 * e]);
+            const float e1 = __uint_as_float(x[8 * u + 2 * e + 1]);
+            pew[e] = pack_bf16(e0, e1);
+            pdw[e] = pack_bf16(dec * e0, dec * e1);
+          }
+          *reinterpret_cast<uint4*>(Es + swz(l, cb + 8 * u)) = pe;
+          *reinterpret_cast<uint4*>(Ed + swz(l, cb + 8 * u)) = pd;
+        }
+        fence_proxy_async_smem();
+      } else {
+        qsc = tail[l];  // read before e_ready: the stage is refilled after MMA2
+      }
+      tc_fence_before();
+      mbar_arrive(&bars->e_ready);
+      // The new state: to Sb (bf16) and, pre-scaled for the next chunk, to TMEM.
+      if (!mbar_wait(&bars->d3_full, c & 1, err, abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      {
+        uint32_t x[32];
+        tmem_ld32(t_s + lane_off + cb, x);
+        tmem_wait_ld_regs(x);
+        if (c + 1 < nchunks) {
+          publish(x, c + 1);
+          tc_fence_before();
+          mbar_arrive(&bars->s_ready);
+        } else if (hT) {
+          float* hrow = hT + ((static_cast<int64_t>(b) * H + h) * DK + r) * DV + v0 + cb;
+#pragma unroll
+          for (int i = 0; i < 32; i += 4)
+            *reinterpret_cast<float4*>(hrow + i) =
+                make_float4(__uint_as_float(x[i]), __uint_as_float(x[i + 1]),
+                            __uint_as_float(x[i + 2]), __uint_as_float(x[i + 3]));
+        }
+      }
+      if (!ok) break;
+      if (!err_rows) {
+        // o (token l) = qsc (Q S)[l] + (QKm err)[l], columns cb..cb+31.
+        if (!mbar_wait(&bars->d2_full, c & 1, err, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        uint32_t x[32], y[32];
+        tmem_ld32(t_d1(c) + lane_off + cb, x);
+        tmem_ld32(t_d2(c) + lane_off + cb, y);
+        tmem_wait_ld_regs(x);
+        tmem_wait_ld_regs(y);
+        const int t = c * kC + l;
+        if (t < T) {
+          uint4* orow = reinterpret_cast<uint4*>(
+              o + ((static_cast<int64_t>(b) * T + t) * H + h) * DV + v0 + cb);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            uint4 pk;
+            uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int i = 8 * u + 2 * e;
+              pw[e] = pack_bf16(fmaf(qsc, __uint_as_float(x[i]), __uint_as_float(y[i])),
+                                fmaf(qsc, __uint_as_float(x[i + 1]), __uint_as_float(y[i + 1])));
+            }
+            orow[u] = pk;
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kScanTcCols);
+  }
+}
+
 template <int DK, int DV>
 int launch_gdn(const void* q, const void* k, const void* v, const float* g, const float* beta,
                const float* h0, void* o, float* hT, void* ws, int B, int T, int H, float scale,
@@ -710,6 +1053,20 @@ int launch_gdn(const void* q, const void* k, const void* v, const float* g, cons
       device_error_ptr());
   int st = launch_status();
   if (st != TILEOPS_OK) return st;
+  if constexpr (DK == 128) {
+    // dk = 128: the tensor-core (tcgen05) scan; its final-state stores are
+    // 16-byte vectors, so it needs an aligned final_state.
+    if (hT == nullptr || aligned16(hT)) {
+      auto k3 = gdn_scan_tc<DV>;
+      if (cudaFuncSetAttribute(k3, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               ScanTcSmem::kAlloc) != cudaSuccess)
+        return TILEOPS_ELAUNCH;
+      k3<<<static_cast<unsigned>(B * H * (DV / kSlice)), kScanTcThreads, ScanTcSmem::kAlloc, s>>>(
+          tq, tk, twk, tu, tqk, static_cast<const __nv_bfloat16*>(ws), h0,
+          static_cast<__nv_bfloat16*>(o), hT, T, H, nchunks, device_error_ptr());
+      return launch_status();
+    }
+  }
   k2<<<static_cast<unsigned>(B * H * (DV / kSlice)), 256, smem2, s>>>(
       tq, tk, twk, tu, tqk, static_cast<const __nv_bfloat16*>(ws), h0,
       static_cast<__nv_bfloat16*>(o), hT, T, H, nchunks, device_error_ptr());

@@ -264,6 +264,13 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, int ab_bf16, int 
          | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+// Same, with the major-ness of A selectable too (16-bit operands may be
+// K- or MN-major on either side).
+__host__ __device__ constexpr uint32_t idesc_f16_major(int M, int N, int ab_bf16, int a_mn_major,
+                                                       int b_mn_major) {
+  return idesc_f16(M, N, ab_bf16, b_mn_major) | (static_cast<uint32_t>(a_mn_major) << 15);
+}
+
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
