@@ -42,6 +42,15 @@ __device__ __forceinline__ float apply_act(float v, int act) {
   return v;
 }
 
+// SiLU of two values with packed fp32x2 arithmetic: v * rcp(1 + 2^(-v log2 e))
+// with ex2.approx / rcp.approx (relative error ~2^-21 each); large negative v
+// gives 1 + e = inf, rcp = 0 and a signed zero.
+__device__ __forceinline__ float2 silu2(float2 v) {
+  const float2 m = fmul2(v, make_float2(-1.4426950408889634f, -1.4426950408889634f));
+  const float2 d = fadd2(make_float2(ex2_approx_f(m.x), ex2_approx_f(m.y)), make_float2(1.0f, 1.0f));
+  return fmul2(v, make_float2(rcp_approx_f(d.x), rcp_approx_f(d.y)));
+}
+
 // ------------------------------------------------------------ packet path
 constexpr int kPkThreads = 256;
 
@@ -51,10 +60,10 @@ constexpr int kPkThreads = 256;
 // 8 outputs when PAD <= 8 and K - PAD <= 9.
 constexpr int kPkPerThread = 4;  // packets per thread (loads issued together)
 
-template <typename T, typename W, int K, int PAD>
+template <typename T, typename W, int K, int PAD, int ACT>
 __global__ void __launch_bounds__(kPkThreads)
     dwconv_packet(const T* __restrict__ x, const W* __restrict__ w, const W* __restrict__ bias,
-                  T* __restrict__ y, int64_t C, int64_t l_in, int64_t l_out, int act,
+                  T* __restrict__ y, int64_t C, int64_t l_in, int64_t l_out,
                   int64_t tiles_per_row) {
   constexpr int V = 8;  // elements per packet (16 bytes of a 2-byte type)
   static_assert(PAD <= V && K - PAD <= V + 1, "halo wider than one packet");
@@ -113,13 +122,18 @@ __global__ void __launch_bounds__(kPkThreads)
         win[2 * V + t] = Cvt<T>::to_f(d.e[t]);
       }
     }
+    // Outputs in pairs: the taps as packed fp32x2 FMAs.
     Pack16<T> out;
 #pragma unroll
-    for (int j = 0; j < V; ++j) {
-      float acc = bv;
+    for (int j = 0; j < V; j += 2) {
+      float2 acc = make_float2(bv, bv);
 #pragma unroll
-      for (int k = 0; k < K; ++k) acc = fmaf(wk[k], win[V + j + k - PAD], acc);
-      out.e[j] = Cvt<T>::from_f(apply_act(acc, act));
+      for (int k = 0; k < K; ++k)
+        acc = ffma2(make_float2(wk[k], wk[k]),
+                    make_float2(win[V + j + k - PAD], win[V + j + 1 + k - PAD]), acc);
+      if constexpr (ACT == TILEOPS_ACT_SILU) acc = silu2(acc);
+      out.e[j] = Cvt<T>::from_f(acc.x);
+      out.e[j + 1] = Cvt<T>::from_f(acc.y);
     }
     if (o0 + V <= l_out) {
       st_stream(yr + o0, out.u);
@@ -137,8 +151,12 @@ int launch_packet(const T* x, const W* w, const W* b, T* y, int64_t c, int64_t l
   const int64_t tiles = (pk_out + per_cta - 1) / per_cta;
   const int64_t grid = rows * tiles;
   if (grid > 0x7fffffffLL) return TILEOPS_EBADSHAPE;
-  dwconv_packet<T, W, K, PAD><<<static_cast<unsigned>(grid), kPkThreads, 0, s>>>(
-      x, w, b, y, c, l_in, l_out, act, tiles);
+  if (act == TILEOPS_ACT_SILU)
+    dwconv_packet<T, W, K, PAD, TILEOPS_ACT_SILU><<<static_cast<unsigned>(grid), kPkThreads, 0, s>>>(
+        x, w, b, y, c, l_in, l_out, tiles);
+  else
+    dwconv_packet<T, W, K, PAD, TILEOPS_ACT_NONE><<<static_cast<unsigned>(grid), kPkThreads, 0, s>>>(
+        x, w, b, y, c, l_in, l_out, tiles);
   return launch_status();
 }
 

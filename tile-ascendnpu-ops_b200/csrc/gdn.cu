@@ -90,14 +90,15 @@ struct Ws {
 };
 
 // =========================================================== kernel 1
-// 128 threads (4 warps), one CTA per (b, h, chunk); three CTAs per SM.
+// 128 threads (4 warps), one CTA per (b, h, chunk); four CTAs per SM.
 // K, Q, V arrive by TMA as 128-byte-swizzled [64][64] bf16 boxes (tokens
 // past T read as zeros).  Shared memory:
-//   Ks [64][DK], Vs [64][DV]   swizzled bf16 (TMA)
+//   Ks [64][DK]                swizzled bf16 (TMA)
 //   Qs [64][DK]                swizzled bf16 (TMA); once QK^T is formed the
 //                              region holds Tf (T in fp32, [64][68]) and then
 //                              Tk, Tv (swizzled bf16 [64][64] each)
-//   As fp32 [64][65]           A, strictly lower
+//   As fp32 [64][65]           A, strictly lower; once T is formed the region
+//                              takes V (swizzled [64][DV] bf16, TMA)
 //   gc, beta, ke = beta e^gc   [64] each
 //   mbarrier + abort flag
 // Tile addressing: 16-byte unit u of row r in a 64-column box at
@@ -143,18 +144,19 @@ struct PrepSmem {
   static constexpr int kKs = 0;
   static constexpr int kQs = kKs + kC * DK * 2;
   static constexpr int kQsBytes = cmax(cmax(kC * DK * 2, kC * kLdTf * 4), 2 * kC * kC * 2);
-  static constexpr int kVs = (kQs + kQsBytes + 1023) & ~1023;
-  static constexpr int kAs = kVs + kC * DV * 2;
-  static constexpr int kGc = kAs + kC * kLdA * 4;
+  // As (fp32 [64][65]) until T is formed, then V (swizzled [64][DV] bf16).
+  static constexpr int kAs = (kQs + kQsBytes + 1023) & ~1023;
+  static constexpr int kVs = kAs;
+  static constexpr int kGc = kAs + cmax(kC * kLdA * 4, kC * DV * 2);
   static constexpr int kBeta = kGc + kC * 4;
   static constexpr int kKe = kBeta + kC * 4;
-  static constexpr int kBar = kKe + kC * 4;
-  static constexpr int kBytes = kBar + 16;
+  static constexpr int kBar = kKe + kC * 4;     // two mbarriers + abort flag
+  static constexpr int kBytes = kBar + 32;
   static constexpr int kAlloc = kBytes + 1024;  // room to align the base to 1 KB
 };
 
 template <int DK, int DV>
-__global__ void __launch_bounds__(128, 3)
+__global__ void __launch_bounds__(128, 4)
     gdn_prepare(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                 const __grid_constant__ CUtensorMap tm_v, const float* __restrict__ g,
                 const float* __restrict__ beta, __nv_bfloat16* __restrict__ ws, int T, int H,
@@ -170,8 +172,9 @@ __global__ void __launch_bounds__(128, 3)
   float* gc = reinterpret_cast<float*>(sm + L::kGc);
   float* bt = reinterpret_cast<float*>(sm + L::kBeta);
   float* ke = reinterpret_cast<float*>(sm + L::kKe);
-  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + L::kBar);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + L::kBar + 8);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + L::kBar);       // K, Q
+  uint64_t* bar_v = reinterpret_cast<uint64_t*>(sm + L::kBar + 8);  // V
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + L::kBar + 16);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g8 = lane >> 2, t2 = (lane & 3) * 2;
@@ -184,20 +187,18 @@ __global__ void __launch_bounds__(128, 3)
 
   if (tid == 0) {
     sm100::mbar_init(bar, 1);
+    sm100::mbar_init(bar_v, 1);
     *abort_flag = 0;
     sm100::fence_mbar_init();
   }
   __syncthreads();
   if (tid == 0) {
-    sm100::mbar_arrive_expect_tx(bar, (2 * DK + DV) * kC * 2);
+    sm100::mbar_arrive_expect_tx(bar, 2 * DK * kC * 2);
 #pragma unroll
     for (int c = 0; c < DK / 64; ++c) {
       sm100::tma_load_4d(sm + L::kKs + c * 8192, &tm_k, bar, c * 64, h, t0, b);
       sm100::tma_load_4d(sm + L::kQs + c * 8192, &tm_q, bar, c * 64, h, t0, b);
     }
-#pragma unroll
-    for (int c = 0; c < DV / 64; ++c)
-      sm100::tma_load_4d(sm + L::kVs + c * 8192, &tm_v, bar, c * 64, h, t0, b);
   }
   if (warp == 0) {
     // inclusive cumsum of g over the 64 tokens: two per lane + warp scan
@@ -310,6 +311,7 @@ __global__ void __launch_bounds__(128, 3)
   // ---- off-diagonal blocks by distance d = i - j: warp p < 4 - d forms
   //   X = sum_{m=j}^{i-1} A_im T_mj,   T_ij = -T_ii X      ((i, j) = (p + d, p))
   // in fp32 on the CUDA cores; lane -> row lane / 2, columns 8 (lane % 2)...
+#pragma unroll
   for (int d = 1; d < 4; ++d) {
     if (warp < 4 - d) {
       const int i = warp + d, j = warp;
@@ -317,7 +319,9 @@ __global__ void __launch_bounds__(128, 3)
       float x[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) x[e] = 0.0f;
-      for (int m = j; m < i; ++m) {
+#pragma unroll
+      for (int mm = 0; mm < d; ++mm) {
+        const int m = j + mm;
 #pragma unroll
         for (int kx = 0; kx < 16; ++kx) {
           const float a = As[(i * 16 + r) * kLdA + m * 16 + kx];
@@ -360,6 +364,14 @@ __global__ void __launch_bounds__(128, 3)
     }
     __syncthreads();
   }
+  // As is dead: V lands in its place while Tk, Tv and Wk are formed.
+  if (tid == 0) {
+    sm100::fence_proxy_async_smem();
+    sm100::mbar_arrive_expect_tx(bar_v, DV * kC * 2);
+#pragma unroll
+    for (int c = 0; c < DV / 64; ++c)
+      sm100::tma_load_4d(sm + L::kVs + c * 8192, &tm_v, bar_v, c * 64, h, t0, b);
+  }
 
   // ---- Tk = T diag(beta e^gc), Tv = T diag(beta) in bf16, swizzled [64][64]
   // each, over the Tf region (read all of Tf first).
@@ -394,12 +406,20 @@ __global__ void __launch_bounds__(128, 3)
   }
   __syncthreads();
 
-  // ---- Wk = Tk K (C x DK), U = Tv V (C x DV): warp w owns rows 16w..16w+15;
-  // T is lower triangular, so k-blocks 0..w.
+  // ---- Wk = Tk K (C x DK), then (once V has landed) U = Tv V (C x DV): warp
+  // w owns rows 16w..16w+15; T is lower triangular, so k-blocks 0..w.
   {
     const int m0 = warp * 16;
 #pragma unroll
     for (int which = 0; which < 2; ++which) {
+      if (which == 1) {
+        const bool v_landed = sm100::mbar_wait(bar_v, 0, err, abort_flag);
+        if (!__syncthreads_and(v_landed)) {
+          if (tid == 0) sm100::mbar_wait(bar_v, 0, nullptr, abort_flag, true);
+          __syncthreads();
+          return;
+        }
+      }
       const int D = which == 0 ? DK : DV;
       const uint32_t tA = sb + L::kQs + which * 8192;
       const uint32_t X = which == 0 ? sK : sV;
