@@ -109,3 +109,28 @@ def test_baseline_config_sampled_heads():
         o_ref, s_ref = ref.gdn_prefill_bthd(q[sl], k[sl], v[sl], g[sl], beta[sl])
         torch.testing.assert_close(o[sl].cpu().float(), o_ref.float(), **TOL)
         torch.testing.assert_close(s[bi : bi + 1, hi : hi + 1].cpu(), s_ref, **TOL)
+
+
+def test_misaligned_final_state_runs_the_register_scan():
+    """dk = 128 normally scans on tcgen05, which stores the final state with
+    16-byte vectors; a final_state pointer off that alignment runs the
+    mma.sync register scan instead.  Both must match the golden."""
+    from tileops import _native as nat
+
+    q, k, v, g, beta = GdnPrefillWorkload(1, 320, 2, 128, 128).gen_inputs()
+    B, T, H, DK = q.shape
+    DV = v.shape[-1]
+    nbytes = nat.lib().tileops_gdn_workspace_bytes(B, T, H, DK, DV)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    o = torch.empty_like(v)
+    buf = torch.zeros(B * H * DK * DV + 1, dtype=torch.float32, device="cuda")
+    hT = buf[1:]  # 4 bytes past a 16-byte boundary
+    nat.launch("tileops_gdn_prefill_fwd", q.device, nat.ptr(q), nat.ptr(k), nat.ptr(v),
+               nat.ptr(g), nat.ptr(beta), nat.ptr(None), nat.ptr(o), nat.ptr(hT), nat.ptr(ws),
+               B, T, H, DK, DV, 64, DK ** -0.5, nat.dtype_code(torch.bfloat16))
+    torch.cuda.synchronize()
+    o_ref, s_ref = ref.gdn_prefill_bthd(q, k, v, g, beta)
+    torch.testing.assert_close(o.cpu().float(), o_ref.float(), **TOL)
+    torch.testing.assert_close(hT.view(B, H, DK, DV).cpu(), s_ref, **TOL)
+    o_tc, s_tc = _run(q, k, v, g, beta)
+    torch.testing.assert_close(o.float(), o_tc.float(), atol=2e-2, rtol=2e-2)
