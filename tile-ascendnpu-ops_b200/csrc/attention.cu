@@ -205,23 +205,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idesc_qk = idesc_f16(kBM, kBN, BF16 ? 1 : 0, 0);
       constexpr uint32_t idesc_pv = idesc_f16(kBM, D, BF16 ? 1 : 0, 1);
       bool ok = mbar_wait(&bars->q_full, 0, p.err, abort_flag);
+      // Descriptors of the tile bases, built once; every k-step's descriptor
+      // is one of these advanced by a compile-time byte offset.
+      const uint64_t q_desc = smem_desc(smem_u32(smem + L::kQ), 16, 1024);
+      const uint64_t k_desc = smem_desc(smem_u32(smem + L::kK), 16, 1024);
+      const uint64_t v_desc = smem_desc(smem_u32(smem + L::kV), kBN * 128, 1024);
       auto issue_s = [&](int t, int j) {  // S_t = Q_t K_j^T
-        const uint32_t q_base = smem_u32(smem + L::kQ + t * kTileBytes);
-        const uint32_t k_base = smem_u32(smem + L::kK + (j % kStages) * kTileBytes);
+        const uint64_t qd = desc_advance(q_desc, t * kTileBytes);
+        const uint64_t kd = desc_advance(k_desc, (j % kStages) * kTileBytes);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off_b = (kk >> 2) * (kBM * 128) + (kk & 3) * 32;
-          mma_f16_ss(tmem + t * 256, smem_desc(q_base + off_b, 16, 1024),
-                     smem_desc(k_base + off_b, 16, 1024), idesc_qk, kk > 0);
+          mma_f16_ss(tmem + t * 256, desc_advance(qd, off_b), desc_advance(kd, off_b), idesc_qk,
+                     kk > 0);
         }
         mma_commit(&bars->s_full[t]);
       };
       auto issue_pv = [&](int t, int j) {  // O_t += P_t V_j
-        const uint32_t v_base = smem_u32(smem + L::kV + (j % kStages) * kTileBytes);
+        const uint64_t vd = desc_advance(v_desc, (j % kStages) * kTileBytes);
+        const uint32_t t_p = tmem + t * 256;
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk)
-          mma_f16_ts(tmem + t * 256 + 128, tmem + t * 256 + kk * 8,
-                     smem_desc(v_base + kk * 16 * 128, kBN * 128, 1024), idesc_pv,
+          mma_f16_ts(t_p + 128, t_p + kk * 8, desc_advance(vd, kk * 16 * 128), idesc_pv,
                      (j > 0 || kk > 0));
       };
       // Prologue: S for block 0 of both tiles.

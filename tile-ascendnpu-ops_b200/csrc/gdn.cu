@@ -857,39 +857,41 @@ __global__ void __launch_bounds__(kScanTcThreads, 1)
     if (lane == 0) {
       constexpr uint32_t id_kmn = idesc_f16_major(128, 64, 1, 0, 1);  // A K-major, B MN-major
       constexpr uint32_t id_mnmn = idesc_f16_major(128, 64, 1, 1, 1);  // A MN-major (K^T)
-      const uint32_t id_base = smem_u32(sm + L::kId);
-      const uint32_t sb_base = smem_u32(sm + L::kSb);
-      const uint32_t es_base = smem_u32(sm + L::kEs);
-      const uint32_t ed_base = smem_u32(sm + L::kEd);
+      // Base descriptors built once; k-steps advance them by constant offsets.
+      const uint64_t id_d = smem_desc(smem_u32(sm + L::kId), 16, 1024);
+      const uint64_t sb_d = smem_desc(smem_u32(sm + L::kSb), 16384, 1024);
+      const uint64_t es_d = smem_desc(smem_u32(sm + L::kEs), 8192, 1024);
+      const uint64_t ed_d = smem_desc(smem_u32(sm + L::kEd), 8192, 1024);
+      const uint64_t st_k = smem_desc(smem_u32(sm), 16, 1024);      // K-major tiles
+      const uint64_t st_mn = smem_desc(smem_u32(sm), 8192, 1024);   // MN-major tiles
       for (int c = 0; c < nchunks; ++c) {
         const int s = c % kTcStages;
-        const uint32_t st = smem_u32(sm + s * L::kStage);
+        const uint32_t so = s * L::kStage;
         const uint32_t d1 = t_d1(c);
         if (!mbar_wait(&bars->full[s], (c / kTcStages) & 1, err, abort_flag)) break;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kC / 16; ++kk)  // D1 = [I ; 0] U
-          mma_f16_ss(d1, smem_desc(id_base + kk * 32, 16, 1024),
-                     smem_desc(st + L::kUQ + kk * 2048, 8192, 1024), id_kmn, kk > 0);
+          mma_f16_ss(d1, desc_advance(id_d, kk * 32),
+                     desc_advance(st_mn, so + L::kUQ + kk * 2048), id_kmn, kk > 0);
         if (!mbar_wait(&bars->s_ready, c & 1, err, abort_flag)) break;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < DK / 16; ++kk)  // D1 += [-Wk ; Q] Sb
-          mma_f16_ss(d1,
-                     smem_desc(st + L::kA1 + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024),
-                     smem_desc(sb_base + kk * 2048, 16384, 1024), id_kmn, 1);
+          mma_f16_ss(d1, desc_advance(st_k, so + L::kA1 + (kk >> 2) * 16384 + (kk & 3) * 32),
+                     desc_advance(sb_d, kk * 2048), id_kmn, 1);
         mma_commit(&bars->d1_full);
         if (!mbar_wait(&bars->e_ready, c & 1, err, abort_flag)) break;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kC / 16; ++kk)  // S += K^T Ed
-          mma_f16_ss(t_s, smem_desc(st + L::kK + kk * 2048, 8192, 1024),
-                     smem_desc(ed_base + kk * 2048, 8192, 1024), id_mnmn, 1);
+          mma_f16_ss(t_s, desc_advance(st_mn, so + L::kK + kk * 2048),
+                     desc_advance(ed_d, kk * 2048), id_mnmn, 1);
         mma_commit(&bars->d3_full);
 #pragma unroll
         for (int kk = 0; kk < kC / 16; ++kk)  // D2 = [U ; QKm] Es
-          mma_f16_ss(t_d2(c), smem_desc(st + L::kUQ + kk * 32, 16, 1024),
-                     smem_desc(es_base + kk * 2048, 8192, 1024), id_kmn, kk > 0);
+          mma_f16_ss(t_d2(c), desc_advance(st_k, so + L::kUQ + kk * 32),
+                     desc_advance(es_d, kk * 2048), id_kmn, kk > 0);
         mma_commit(&bars->d2_full);
         mma_commit(&bars->empty[s]);
       }

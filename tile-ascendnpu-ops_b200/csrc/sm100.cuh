@@ -253,6 +253,16 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes
   return d;
 }
 
+// The same descriptor `bytes` (a multiple of 16) further on: only the 14-bit
+// start-address field (bits 0-13, in 16-byte units) changes, and shared
+// memory addresses stay below 256 KB, so a 32-bit add on the low word never
+// carries.  Building each k-step's descriptor this way from one base costs a
+// single integer add, which matters because one thread issues every MMA.
+__device__ __forceinline__ uint64_t desc_advance(uint64_t d, uint32_t bytes) {
+  const uint32_t lo = static_cast<uint32_t>(d) + (bytes >> 4);
+  return (d & 0xffffffff00000000ull) | lo;
+}
+
 // Instruction descriptor, kind::f16: fp32 accumulate, dense.
 // ab_bf16: 1 = bf16 operands, 0 = fp16.  b_mn_major: B is MN-major.
 __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, int ab_bf16, int b_mn_major) {
