@@ -165,24 +165,11 @@ struct FastDivU32 {
   }
 };
 
-// CTAs of `kernel` that fit on one SM at `threads` threads per CTA (at least 1).
-template <typename Kernel>
-int resident_ctas(Kernel kernel, int threads, size_t smem = 0) {
-  int n = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, smem) != cudaSuccess ||
-      n < 1)
-    n = 1;
-  return n;
-}
-
-// Grid of a grid-stride streaming kernel: enough CTAs for the work, at most
-// one full wave (every SM holding `resident` CTAs), so no CTA waits for a
-// second wave while others run.
-inline unsigned stream_grid_resident(int64_t work, int64_t per_cta, int resident) {
-  int64_t need = (work + per_cta - 1) / per_cta;
-  const int64_t cap = static_cast<int64_t>(sm_count()) * resident;
-  if (need < 1) need = 1;
-  return static_cast<unsigned>(need < cap ? need : cap);
+// Grid of a single-pass streaming kernel: one CTA per `per_cta` units of
+// work (at least one CTA, so block 0 can finish a ragged tail).
+inline unsigned single_pass_grid(int64_t units, int64_t per_cta) {
+  const int64_t g = (units + per_cta - 1) / per_cta;
+  return static_cast<unsigned>(g < 1 ? 1 : g);
 }
 
 inline unsigned stream_grid(int64_t work, int64_t per_cta, int waves) {

@@ -76,6 +76,8 @@ struct GeluTanhF {
 // Packet p of the flattened (row, packet-in-row) index space sits in row
 // p / pk_per_row; the division is a FastDivU32 when the index space fits in
 // 32 bits (every shape up to 2^32 packets), a 64-bit division otherwise.
+// Single pass: CTA b owns packets [b * kThreads * kUnroll, (b + 1) * ...),
+// each thread kUnroll of them kThreads apart, all loads in flight together.
 template <typename T, typename F, bool k32>
 __global__ void __launch_bounds__(kThreads)
     gated_vec(const T* __restrict__ x, T* __restrict__ y, int64_t M, int64_t N, F f,
@@ -83,7 +85,6 @@ __global__ void __launch_bounds__(kThreads)
   constexpr int V = 16 / sizeof(T);
   const int64_t pk_per_row = N / V;
   const int64_t total = M * pk_per_row;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
   auto row_of = [&](int64_t p) -> int64_t {
     if constexpr (k32) {
       return rowdiv.div(static_cast<uint32_t>(p));
@@ -91,13 +92,14 @@ __global__ void __launch_bounds__(kThreads)
       return p / pk_per_row;
     }
   };
-  int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
-  for (; i + (kUnroll - 1) * stride < total; i += kUnroll * stride) {
-    Pack16<T> g[kUnroll], v[kUnroll];
-    int64_t out_off[kUnroll];
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * (kThreads * kUnroll) + threadIdx.x;
+  Pack16<T> g[kUnroll], v[kUnroll];
+  int64_t out_off[kUnroll];
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const int64_t p = i + u * stride;
+  for (int u = 0; u < kUnroll; ++u) {
+    const int64_t p = base + u * kThreads;
+    out_off[u] = -1;
+    if (p < total) {
       const int64_t r = row_of(p);
       const int64_t c = (p - r * pk_per_row) * V;
       const T* row = x + r * 2 * N;
@@ -105,31 +107,21 @@ __global__ void __launch_bounds__(kThreads)
       v[u].u = ld_stream(row + N + c);
       out_off[u] = r * N + c;
     }
+  }
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      after_loads(g[u].u);
-      after_loads(v[u].u);
-    }
+  for (int u = 0; u < kUnroll; ++u) {
+    after_loads(g[u].u);
+    after_loads(v[u].u);
+  }
 #pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
+  for (int u = 0; u < kUnroll; ++u) {
+    if (out_off[u] >= 0) {
       Pack16<T> o;
 #pragma unroll
       for (int e = 0; e < V; ++e)
         o.e[e] = Cvt<T>::from_f(f(Cvt<T>::to_f(g[u].e[e]), Cvt<T>::to_f(v[u].e[e])));
       st_stream(y + out_off[u], o.u);
     }
-  }
-  for (; i < total; i += stride) {
-    const int64_t r = row_of(i);
-    const int64_t c = (i - r * pk_per_row) * V;
-    const T* row = x + r * 2 * N;
-    Pack16<T> g, v, o;
-    g.u = ld_stream(row + c);
-    v.u = ld_stream(row + N + c);
-#pragma unroll
-    for (int e = 0; e < V; ++e)
-      o.e[e] = Cvt<T>::from_f(f(Cvt<T>::to_f(g.e[e]), Cvt<T>::to_f(v.e[e])));
-    st_stream(y + r * N + c, o.u);
   }
 }
 
@@ -154,17 +146,13 @@ int launch_gated_t(const void* x, void* y, int64_t M, int64_t N, F f, cudaStream
   T* yp = static_cast<T*>(y);
   if (N % V == 0 && aligned16(x) && aligned16(y)) {
     const int64_t total = M * (N / V);
-    static const int res32 = resident_ctas(gated_vec<T, F, true>, kThreads);
-    static const int res64 = resident_ctas(gated_vec<T, F, false>, kThreads);
-    const unsigned grid32 = stream_grid_resident(total, kThreads * kUnroll, res32);
-    // 32-bit path: every packet index, including the last unrolled group's
-    // overshoot (< total + kUnroll * grid * kThreads), stays below 2^32.
-    if (total + static_cast<int64_t>(kUnroll) * grid32 * kThreads < (int64_t{1} << 32))
-      gated_vec<T, F, true><<<grid32, kThreads, 0, s>>>(
+    const unsigned grid = single_pass_grid(total, kThreads * kUnroll);
+    // 32-bit path: every packet index (< grid * kThreads * kUnroll) below 2^32.
+    if (static_cast<int64_t>(grid) * kThreads * kUnroll <= (int64_t{1} << 32))
+      gated_vec<T, F, true><<<grid, kThreads, 0, s>>>(
           xp, yp, M, N, f, FastDivU32(static_cast<uint32_t>(N / V)));
     else
-      gated_vec<T, F, false><<<stream_grid_resident(total, kThreads * kUnroll, res64), kThreads,
-                               0, s>>>(xp, yp, M, N, f, FastDivU32(1));
+      gated_vec<T, F, false><<<grid, kThreads, 0, s>>>(xp, yp, M, N, f, FastDivU32(1));
   } else {
     gated_scalar<T, F><<<stream_grid(M * N, kThreads, 8), kThreads, 0, s>>>(xp, yp, M, N, f);
   }
