@@ -78,11 +78,23 @@ __global__ void __launch_bounds__(kPkThreads)
   // Packet i of this thread: consecutive lanes own consecutive packets, so
   // a lane's neighbours in the row are its neighbours in the warp.
   const int64_t pk0 = tile * (kPkThreads * kPkPerThread) + threadIdx.x;
-  uint4 cur[kPkPerThread];
+  uint4 cur[kPkPerThread], edge[kPkPerThread];
 #pragma unroll
   for (int i = 0; i < kPkPerThread; ++i) {
     const int64_t pk = pk0 + i * kPkThreads;
     cur[i] = (pk < in_pk) ? ld_stream(xr + pk * V) : zero;
+  }
+  // Warp-edge lanes fetch the packet beyond their warp's run (lane 0 the one
+  // before, lane 31 the one after) together with the main loads; the
+  // adjacent warp reads it at the same time, so it is an L2 hit.
+#pragma unroll
+  for (int i = 0; i < kPkPerThread; ++i) {
+    const int64_t pk = pk0 + i * kPkThreads;
+    edge[i] = zero;
+    if (PAD > 0 && lane == 0 && pk >= 1 && pk - 1 < in_pk)
+      edge[i] = __ldg(reinterpret_cast<const uint4*>(xr) + pk - 1);
+    if (K - 1 - PAD > 0 && lane == 31 && pk + 1 < in_pk)
+      edge[i] = __ldg(reinterpret_cast<const uint4*>(xr) + pk + 1);
   }
   float wk[K];
 #pragma unroll
@@ -100,13 +112,8 @@ __global__ void __launch_bounds__(kPkThreads)
     next.y = __shfl_down_sync(0xffffffffu, cur[i].y, 1);
     next.z = __shfl_down_sync(0xffffffffu, cur[i].z, 1);
     next.w = __shfl_down_sync(0xffffffffu, cur[i].w, 1);
-    // Warp-edge lanes fetch the neighbour packet themselves (the adjacent
-    // warp reads it at the same time, so it is an L2 hit).
-    if (PAD > 0 && lane == 0)
-      prev = (pk >= 1 && pk - 1 < in_pk) ? __ldg(reinterpret_cast<const uint4*>(xr) + pk - 1)
-                                         : zero;
-    if (K - 1 - PAD > 0 && lane == 31)
-      next = (pk + 1 < in_pk) ? __ldg(reinterpret_cast<const uint4*>(xr) + pk + 1) : zero;
+    if (PAD > 0 && lane == 0) prev = edge[i];
+    if (K - 1 - PAD > 0 && lane == 31) next = edge[i];
     const int64_t o0 = pk * V;
     if (o0 >= l_out) continue;
     float win[3 * V];  // win[t] = x[o0 - V + t]
