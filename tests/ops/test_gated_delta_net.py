@@ -134,3 +134,13 @@ def test_misaligned_final_state_runs_the_register_scan():
     torch.testing.assert_close(hT.view(B, H, DK, DV).cpu(), s_ref, **TOL)
     o_tc, s_tc = _run(q, k, v, g, beta)
     torch.testing.assert_close(o.float(), o_tc.float(), atol=2e-2, rtol=2e-2)
+
+
+def test_strong_decay_takes_the_exact_exponentials():
+    """A chunk whose cumulative log-decay passes -80 forms e^(gc_l - gc_s) per
+    entry instead of e^gc_l * e^-gc_s (whose factors would overflow fp32);
+    chunks of both kinds in one call."""
+    q, k, v, g, beta = GdnPrefillWorkload(1, 256, 2, 128, 128).gen_inputs()
+    g = g.clone()
+    g[:, 64:128] = -2.5  # the second chunk reaches gc = -160
+    _check(q, k, v, g, beta)

@@ -150,7 +150,9 @@ struct PrepSmem {
   static constexpr int kGc = kAs + cmax(kC * kLdA * 4, kC * DV * 2);
   static constexpr int kBeta = kGc + kC * 4;
   static constexpr int kKe = kBeta + kC * 4;
-  static constexpr int kBar = kKe + kC * 4;     // two mbarriers + abort flag
+  static constexpr int kEgp = kKe + kC * 4;     // e^gc
+  static constexpr int kEgm = kEgp + kC * 4;    // e^-gc, and the factor flag after it
+  static constexpr int kBar = kEgm + kC * 4 + 16;  // two mbarriers + abort flag
   static constexpr int kBytes = kBar + 32;
   static constexpr int kAlloc = kBytes + 1024;  // room to align the base to 1 KB
 };
@@ -158,7 +160,8 @@ struct PrepSmem {
 template <int DK, int DV>
 __global__ void __launch_bounds__(128, 4)
     gdn_prepare(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                const __grid_constant__ CUtensorMap tm_v, const float* __restrict__ g,
+                const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_wk,
+                const __grid_constant__ CUtensorMap tm_u, const float* __restrict__ g,
                 const float* __restrict__ beta, __nv_bfloat16* __restrict__ ws, int T, int H,
                 int nchunks, float scale, int* err) {
   using L = PrepSmem<DK, DV>;
@@ -172,6 +175,9 @@ __global__ void __launch_bounds__(128, 4)
   float* gc = reinterpret_cast<float*>(sm + L::kGc);
   float* bt = reinterpret_cast<float*>(sm + L::kBeta);
   float* ke = reinterpret_cast<float*>(sm + L::kKe);
+  float* egp = reinterpret_cast<float*>(sm + L::kEgp);
+  float* egm = reinterpret_cast<float*>(sm + L::kEgm);
+  int* fact_flag = reinterpret_cast<int*>(sm + L::kEgm + kC * 4);
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + L::kBar);       // K, Q
   uint64_t* bar_v = reinterpret_cast<uint64_t*>(sm + L::kBar + 8);  // V
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + L::kBar + 16);
@@ -222,10 +228,21 @@ __global__ void __launch_bounds__(128, 4)
       if (lane >= o) incl += up;
     }
     const float excl = incl - pair;
-    gc[2 * lane] = excl + g0;
-    gc[2 * lane + 1] = incl;
+    const float c0 = excl + g0, c1 = incl;
+    gc[2 * lane] = c0;
+    gc[2 * lane + 1] = c1;
     bt[2 * lane] = b0;
     bt[2 * lane + 1] = b1;
+    // G[l, s] = e^(gc_l - gc_s) may be formed as e^gc_l * e^-gc_s when every
+    // |gc| of the chunk is below 80 (both factors then stay finite in fp32).
+    float amax = fmaxf(fabsf(c0), fabsf(c1));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    egp[2 * lane] = __expf(c0);
+    egp[2 * lane + 1] = __expf(c1);
+    egm[2 * lane] = __expf(-c0);
+    egm[2 * lane + 1] = __expf(-c1);
+    if (lane == 0) *fact_flag = amax < 80.0f ? 1 : 0;
   }
   // Every thread waits for the tiles (bounded); the CTA proceeds only if all
   // saw them land, otherwise it lets any copy in flight finish and leaves.
@@ -264,15 +281,22 @@ __global__ void __launch_bounds__(128, 4)
         }
       }
     }
+    const bool fact = *fact_flag != 0;
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
       const int l = m0 + g8 + half * 8;
-      const float gl = gc[l], bl = bt[l];
+      const float gl = gc[l], bl = bt[l], el = egp[l];
 #pragma unroll
       for (int n = 0; n < 8; ++n) {
         const int s = n * 8 + t2;
-        const float d0 = s <= l ? __expf(gl - gc[s]) : 0.0f;
-        const float d1 = s + 1 <= l ? __expf(gl - gc[s + 1]) : 0.0f;
+        float d0, d1;
+        if (fact) {
+          d0 = s <= l ? el * egm[s] : 0.0f;
+          d1 = s + 1 <= l ? el * egm[s + 1] : 0.0f;
+        } else {
+          d0 = s <= l ? __expf(gl - gc[s]) : 0.0f;
+          d1 = s + 1 <= l ? __expf(gl - gc[s + 1]) : 0.0f;
+        }
         As[l * kLdA + s] = s < l ? bl * d0 * ak[n][half * 2] : 0.0f;
         As[l * kLdA + s + 1] = s + 1 < l ? bl * d1 * ak[n][half * 2 + 1] : 0.0f;
         *reinterpret_cast<uint32_t*>(wsc + W::kQK + l * kC + s) =
@@ -407,7 +431,10 @@ __global__ void __launch_bounds__(128, 4)
   __syncthreads();
 
   // ---- Wk = Tk K (C x DK), then (once V has landed) U = Tv V (C x DV): warp
-  // w owns rows 16w..16w+15; T is lower triangular, so k-blocks 0..w.
+  // w owns rows 16w..16w+15; T is lower triangular, so k-blocks 0..w.  Each
+  // result is staged in shared memory (swizzled [64][64] boxes, the freed K
+  // tile for -Wk, the freed Tk / Tv tile for U) and written by TMA stores, so
+  // the workspace sees whole 128-byte lines.
   {
     const int m0 = warp * 16;
 #pragma unroll
@@ -415,42 +442,64 @@ __global__ void __launch_bounds__(128, 4)
       if (which == 1) {
         const bool v_landed = sm100::mbar_wait(bar_v, 0, err, abort_flag);
         if (!__syncthreads_and(v_landed)) {
-          if (tid == 0) sm100::mbar_wait(bar_v, 0, nullptr, abort_flag, true);
+          if (tid == 0) {
+            sm100::mbar_wait(bar_v, 0, nullptr, abort_flag, true);
+            sm100::bulk_wait_read_all();
+          }
           __syncthreads();
           return;
         }
       }
+      constexpr int kMaxD = DK > DV ? DK : DV;
       const int D = which == 0 ? DK : DV;
       const uint32_t tA = sb + L::kQs + which * 8192;
       const uint32_t X = which == 0 ? sK : sV;
-      __nv_bfloat16* out = wsc + (which == 0 ? W::kWk : W::kU);
-      for (int n0 = 0; n0 < D; n0 += 64) {
-        float acc[8][4];
+      float acc[kMaxD / 64][8][4];
 #pragma unroll
-        for (int n = 0; n < 8; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
+      for (int nb = 0; nb < kMaxD / 64; ++nb) {
+        if (nb * 64 >= D) break;
+#pragma unroll
+        for (int n = 0; n < 8; ++n)
+          acc[nb][n][0] = acc[nb][n][1] = acc[nb][n][2] = acc[nb][n][3] = 0.0f;
         for (int kk = 0; kk <= warp; ++kk) {
           uint32_t a[4];
           sfrag_a(a, tA, m0, kk * 16);
 #pragma unroll
           for (int n = 0; n < 8; n += 2) {
             uint32_t bb[4];
-            sfrag_b_kn(bb, X, kk * 16, n0 + n * 8);
-            mma_bf16(acc[n], a, bb[0], bb[1]);
-            mma_bf16(acc[n + 1], a, bb[2], bb[3]);
+            sfrag_b_kn(bb, X, kk * 16, nb * 64 + n * 8);
+            mma_bf16(acc[nb][n], a, bb[0], bb[1]);
+            mma_bf16(acc[nb][n + 1], a, bb[2], bb[3]);
           }
         }
-        // The workspace keeps -Wk (the scans add it) and U.
-        const float sg = which == 0 ? -1.0f : 1.0f;
+      }
+      __syncthreads();  // every read of the tile the result is staged into is done
+      // The workspace keeps -Wk (the scans add it) and U.
+      uint8_t* stage = sm + (which == 0 ? L::kKs : L::kQs);
+      const float sg = which == 0 ? -1.0f : 1.0f;
+#pragma unroll
+      for (int nb = 0; nb < kMaxD / 64; ++nb) {
+        if (nb * 64 >= D) break;
 #pragma unroll
         for (int n = 0; n < 8; ++n) {
-          const int l = m0 + g8, c = n0 + n * 8 + t2;
-          *reinterpret_cast<uint32_t*>(out + l * D + c) =
-              pack_bf16(sg * acc[n][0], sg * acc[n][1]);
-          *reinterpret_cast<uint32_t*>(out + (l + 8) * D + c) =
-              pack_bf16(sg * acc[n][2], sg * acc[n][3]);
+          const int l = m0 + g8, c0 = n * 8;  // 8-column unit within the 64-wide box
+          uint8_t* box = stage + nb * 8192;
+          *reinterpret_cast<uint32_t*>(box + swz(l, c0) + t2 * 2) =
+              pack_bf16(sg * acc[nb][n][0], sg * acc[nb][n][1]);
+          *reinterpret_cast<uint32_t*>(box + swz(l + 8, c0) + t2 * 2) =
+              pack_bf16(sg * acc[nb][n][2], sg * acc[nb][n][3]);
         }
       }
+      sm100::fence_proxy_async_smem();
+      __syncthreads();
+      if (tid == 0) {
+        for (int nb = 0; nb * 64 < D; ++nb)
+          sm100::tma_store_3d(which == 0 ? &tm_wk : &tm_u, stage + nb * 8192, nb * 64, 0,
+                              static_cast<int>(blockIdx.x));
+        sm100::bulk_commit();
+      }
     }
+    if (tid == 0) sm100::bulk_wait_read_all();  // shared memory stays valid until read
   }
 }
 
@@ -1071,7 +1120,7 @@ int launch_gdn(const void* q, const void* k, const void* v, const float* g, cons
   const int64_t grid1 = static_cast<int64_t>(B) * H * nchunks;
   if (grid1 > 0x7fffffffLL) return TILEOPS_EBADSHAPE;
   k1<<<static_cast<unsigned>(grid1), 128, smem1, s>>>(
-      tq, tk, tv, g, beta, static_cast<__nv_bfloat16*>(ws), T, H, nchunks, scale,
+      tq, tk, tv, twk, tu, g, beta, static_cast<__nv_bfloat16*>(ws), T, H, nchunks, scale,
       device_error_ptr());
   int st = launch_status();
   if (st != TILEOPS_OK) return st;
