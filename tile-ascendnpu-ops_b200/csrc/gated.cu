@@ -20,16 +20,6 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kUnroll = 4;  // packet pairs in flight per thread
 
-__device__ __forceinline__ float rcp_approx(float x) {
-  float y;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-__device__ __forceinline__ float ex2_approx(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
 
 // erf by Abramowitz & Stegun, Handbook of Mathematical Functions, formula
 // 7.1.26 (Hastings' rational approximation): for a = |x|,
@@ -40,20 +30,20 @@ __device__ __forceinline__ float ex2_approx(float x) {
 // Limits: erf(+-inf) = +-1 (t = 0, exp = 0) and NaN propagates.
 __device__ __forceinline__ float erf_as7126(float x) {
   const float a = fabsf(x);
-  const float t = rcp_approx(fmaf(0.3275911f, a, 1.0f));
+  const float t = rcp_approx_f(fmaf(0.3275911f, a, 1.0f));
   float poly = fmaf(t, 1.061405429f, -1.453152027f);
   poly = fmaf(t, poly, 1.421413741f);
   poly = fmaf(t, poly, -0.284496736f);
   poly = fmaf(t, poly, 0.254829592f);
   poly *= t;
-  const float e = ex2_approx(-(a * a) * 1.4426950408889634f);  // exp(-a^2)
+  const float e = ex2_approx_f(-(a * a) * 1.4426950408889634f);  // exp(-a^2)
   return copysignf(fmaf(-poly, e, 1.0f), x);
 }
 
 // tanh(u) = 1 - 2 / (1 + exp(2u)); saturates to +-1 for large |u| and has an
 // absolute error of a few 1e-7, which GELU multiplies by 0.5 g.
 __device__ __forceinline__ float tanh_via_exp(float u) {
-  return fmaf(-2.0f, rcp_approx(1.0f + ex2_approx(u * 2.8853900817779268f)), 1.0f);
+  return fmaf(-2.0f, rcp_approx_f(1.0f + ex2_approx_f(u * 2.8853900817779268f)), 1.0f);
 }
 
 struct GeluErfF {
