@@ -53,9 +53,10 @@ extern "C" {
 int tileops_abi_version(void);
 /* Static, human-readable text for a status code. */
 const char* tileops_status_string(int status);
-/* Status of the last bounded device-side wait, read back by the host after
- * the stream is synchronised (0 = every wait completed).  Used by the
- * kernels that spin on an mbarrier (attention, gated delta net). */
+/* Device-side error word, read back by the host after the stream is
+ * synchronised: 0 = none; 1 = a bounded mbarrier wait timed out (attention,
+ * gated delta net); 2 = a malformed cu_seqlens was passed to
+ * tileops_gdn_prefill_varlen_fwd.  The first code set is kept until cleared. */
 int tileops_device_error_flag(void* stream, int clear);
 
 /* ---- elementwise unary (flat, n elements; y may not alias x) ----------- */
@@ -189,6 +190,34 @@ int tileops_gdn_prefill_fwd(const void* q, const void* k, const void* v, const f
                             float* final_state, void* workspace, int64_t batch, int64_t seq_len,
                             int64_t heads, int64_t dim_k, int64_t dim_v, int64_t chunk_size,
                             double scale, int dtype, void* stream);
+
+/* Bytes of scratch workspace tileops_gdn_prefill_varlen_fwd needs: the WY
+ * factors of (total_len / 64 + num_seqs) chunk slots per head plus a
+ * chunk -> sequence table of as many int32, or -1 for an unsupported shape. */
+int64_t tileops_gdn_varlen_workspace_bytes(int64_t total_len, int64_t num_seqs, int64_t heads,
+                                           int64_t dim_k, int64_t dim_v);
+
+/* Variable-length form of tileops_gdn_prefill_fwd (the fla `cu_seqlens`
+ * convention, batch 1): num_seqs sequences packed along one token axis,
+ * sequence n being rows [cu_seqlens[n], cu_seqlens[n+1]) of q, k (total_len,
+ * H, dk), v, o (total_len, H, dv), g, beta (total_len, H).  cu_seqlens is an
+ * int32 DEVICE array of num_seqs + 1 offsets with cu_seqlens[0] = 0,
+ * non-decreasing, cu_seqlens[num_seqs] = total_len (empty sequences allowed);
+ * it is never copied to the host, so the call does not synchronise.  A
+ * cu_seqlens that breaks these rules cannot make the kernels access memory
+ * out of range (offsets are clamped) but gives meaningless results, and the
+ * device error flag reads 2 (tileops_device_error_flag).  initial_state
+ * (NULL = zeros) and final_state (NULL = not written) are (num_seqs, H, dk,
+ * dv) fp32; each sequence starts from its own initial state.  `workspace`
+ * holds tileops_gdn_varlen_workspace_bytes() bytes, 16-byte aligned.  Same
+ * sizes, dtype and chunk rules as tileops_gdn_prefill_fwd; no reference
+ * counterpart (the signature follows fla chunk_gated_delta_rule). */
+int tileops_gdn_prefill_varlen_fwd(const void* q, const void* k, const void* v, const float* g,
+                                   const float* beta, const int32_t* cu_seqlens,
+                                   int64_t num_seqs, const float* initial_state, void* o,
+                                   float* final_state, void* workspace, int64_t total_len,
+                                   int64_t heads, int64_t dim_k, int64_t dim_v,
+                                   int64_t chunk_size, double scale, int dtype, void* stream);
 
 /* Same as tileops_gdn_prefill_fwd, but allocates nothing and takes no
  * workspace: for callers that cannot allocate device memory when they call

@@ -235,3 +235,33 @@ def gdn_prefill_bthd(q, k, v, g, beta, scale: Optional[float] = None, initial_st
     o, s = gdn_sequential(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
                           g.transpose(1, 2), beta.transpose(1, 2), s0, scale)
     return o.transpose(1, 2).contiguous().to(v.dtype), s
+
+
+def gdn_prefill_varlen(q, k, v, g, beta, cu_seqlens, scale: Optional[float] = None,
+                       initial_state=None):
+    """The GDN golden on packed variable-length input (fla's ``cu_seqlens``).
+
+    q, k ``(1, T, H, Dk)``, v ``(1, T, H, Dv)``, g / beta ``(1, T, H)`` hold N
+    sequences, sequence n being tokens ``cu_seqlens[n]:cu_seqlens[n + 1]``;
+    initial_state ``(N, H, Dk, Dv)`` or None.  Every sequence runs the
+    sequential recurrence (golden_gdn_sequential,
+    examples/gdn_prefill/probe/gdn_prefill_probe.py:60-77) from its own initial
+    state.  Returns ``(o (1, T, H, Dv), final_state (N, H, Dk, Dv) fp32)``.
+    """
+    q, k, v, g, beta = map(_cpu, (q, k, v, g, beta))
+    cu = [int(x) for x in _cpu(cu_seqlens).tolist()]
+    heads, dk, dv = q.shape[2], q.shape[3], v.shape[3]
+    o = torch.zeros(v.shape, dtype=v.dtype)
+    finals = []
+    for n in range(len(cu) - 1):
+        a, b = cu[n], cu[n + 1]
+        h0 = None if initial_state is None else _cpu(initial_state)[n:n + 1]
+        if b == a:
+            finals.append(torch.zeros(1, heads, dk, dv) if h0 is None else h0.float().clone())
+            continue
+        o_n, s_n = gdn_prefill_bthd(q[:, a:b], k[:, a:b], v[:, a:b], g[:, a:b], beta[:, a:b],
+                                    scale, h0)
+        o[:, a:b] = o_n
+        finals.append(s_n)
+    final = torch.cat(finals, 0) if finals else torch.zeros(0, heads, dk, dv)
+    return o, final

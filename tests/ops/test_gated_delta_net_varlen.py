@@ -1,0 +1,156 @@
+"""GPU parity of the variable-length (``cu_seqlens``) Gated DeltaNet prefill.
+
+Packed sequences (fla's convention: batch 1, N sequences along the token
+axis, N + 1 offsets) must give, per sequence, what the sequential golden
+(examples/gdn_prefill/probe/gdn_prefill_probe.py:60-77, restated in the
+oracle as gdn_prefill_varlen) gives from that sequence's own initial state,
+with the 16-bit tolerance atol = rtol = 1e-2.  Because a chunk never mixes
+two sequences (the rows of a sequence's last chunk past its end are zeroed
+after the load), the packed call must also equal separate calls on each
+sequence bit for bit, and a uniform batch fed as equal-length packed
+sequences must equal the batched call bit for bit.
+"""
+
+import pytest
+import torch
+
+from oracle import reference as ref
+from tileops import _native as nat
+from tileops.ops.linear_attention import GatedDeltaNetPrefillFwdOp
+from tileops.workloads.linear_attention import GdnPrefillWorkload
+
+pytestmark = pytest.mark.gpu
+
+TOL = dict(atol=1e-2, rtol=1e-2)
+
+
+def _cu(lengths):
+    cu = [0]
+    for n in lengths:
+        cu.append(cu[-1] + n)
+    return torch.tensor(cu, dtype=torch.int32, device="cuda")
+
+
+def _packed(lengths, heads, dk, dv, with_h0=True, seed=0):
+    torch.manual_seed(seed)
+    total = sum(lengths)
+    q, k, v, g, beta = GdnPrefillWorkload(1, total, heads, dk, dv).gen_inputs()
+    h0 = (torch.randn(len(lengths), heads, dk, dv, device="cuda") * 0.1) if with_h0 else None
+    return q, k, v, g, beta, h0
+
+
+def _run_varlen(q, k, v, g, beta, cu, h0=None):
+    _, total, heads, dk = q.shape
+    op = GatedDeltaNetPrefillFwdOp(1, total, heads, dk, v.shape[-1])
+    return op(q, k, v, g, beta, h0, cu_seqlens=cu)
+
+
+def _run_one(q, k, v, g, beta, h0=None):
+    b, t, h, dk = q.shape
+    return GatedDeltaNetPrefillFwdOp(b, t, h, dk, v.shape[-1])(q, k, v, g, beta, h0)
+
+
+@pytest.mark.parametrize("lengths, dk, dv", [
+    ([1, 64, 0, 135, 63, 64, 129, 7], 128, 128),
+    ([200, 56, 3], 64, 64),
+    ([65, 0, 191], 128, 64),
+    ([127, 2], 64, 128),
+])
+def test_matches_golden(lengths, dk, dv):
+    q, k, v, g, beta, h0 = _packed(lengths, 2, dk, dv)
+    cu = _cu(lengths)
+    o, s = _run_varlen(q, k, v, g, beta, cu, h0)
+    o_ref, s_ref = ref.gdn_prefill_varlen(q, k, v, g, beta, cu, None, h0)
+    torch.testing.assert_close(o.cpu().float(), o_ref.float(), **TOL)
+    torch.testing.assert_close(s.cpu(), s_ref, **TOL)
+
+
+@pytest.mark.parametrize("dk", [128, 64])
+def test_equals_separate_calls(dk):
+    lengths = [100, 64, 1, 0, 250, 37]
+    q, k, v, g, beta, h0 = _packed(lengths, 3, dk, dk)
+    cu = _cu(lengths)
+    o, s = _run_varlen(q, k, v, g, beta, cu, h0)
+    a = 0
+    for n, ln in enumerate(lengths):
+        if ln == 0:
+            assert torch.equal(s[n], h0[n])
+            continue
+        sl = slice(a, a + ln)
+        o_n, s_n = _run_one(q[:, sl], k[:, sl], v[:, sl], g[:, sl], beta[:, sl], h0[n:n + 1])
+        assert torch.equal(o[:, sl], o_n), f"sequence {n}"
+        assert torch.equal(s[n:n + 1], s_n), f"sequence {n}"
+        a += ln
+
+
+def test_uniform_batch_as_packed_sequences():
+    b, t = 3, 200
+    q, k, v, g, beta = GdnPrefillWorkload(b, t, 2, 128, 128).gen_inputs()
+    o_b, s_b = _run_one(q, k, v, g, beta)
+    flat = lambda x: x.reshape(1, b * t, *x.shape[2:])  # noqa: E731
+    o_p, s_p = _run_varlen(flat(q), flat(k), flat(v), flat(g), flat(beta), _cu([t] * b))
+    assert torch.equal(flat(o_b), o_p)
+    assert torch.equal(s_b, s_p)
+
+
+def test_neighbour_tokens_never_leak():
+    """Inf keys in one sequence leave the sequences around it unchanged: the
+    padding rows of a partial chunk are zeroed, not multiplied by zero."""
+    lengths = [70, 40, 90]
+    q, k, v, g, beta, h0 = _packed(lengths, 2, 128, 128)
+    cu = _cu(lengths)
+    o0, s0 = _run_varlen(q, k, v, g, beta, cu, h0)
+    k2 = k.clone()
+    k2[:, 70:110] = float("inf")  # all of sequence 1
+    v2 = v.clone()
+    v2[:, 70:110] = float("nan")
+    o1, s1 = _run_varlen(q, k2, v2, g, beta, cu, h0)
+    for sl, n in ((slice(0, 70), 0), (slice(110, 200), 2)):
+        assert torch.equal(o0[:, sl], o1[:, sl])
+        assert torch.equal(s0[n], s1[n])
+
+
+def test_all_sequences_empty():
+    h0 = torch.randn(3, 2, 128, 128, device="cuda")
+    e = torch.empty(1, 0, 2, 128, dtype=torch.bfloat16, device="cuda")
+    ge = torch.empty(1, 0, 2, device="cuda")
+    op = GatedDeltaNetPrefillFwdOp(1, 0, 2, 128, 128)
+    o, s = op(e, e, e, ge, ge, h0, cu_seqlens=_cu([0, 0, 0]))
+    assert o.shape == (1, 0, 2, 128) and torch.equal(s, h0)
+    _, s_zero = op(e, e, e, ge, ge, None, cu_seqlens=_cu([0, 0, 0]))
+    assert torch.count_nonzero(s_zero) == 0
+
+
+def test_int64_offsets_accepted():
+    lengths = [33, 95]
+    q, k, v, g, beta, h0 = _packed(lengths, 1, 128, 128)
+    o32, s32 = _run_varlen(q, k, v, g, beta, _cu(lengths), h0)
+    o64, s64 = _run_varlen(q, k, v, g, beta, _cu(lengths).long(), h0)
+    assert torch.equal(o32, o64) and torch.equal(s32, s64)
+
+
+def test_malformed_offsets_set_the_device_error_flag():
+    """Decreasing offsets are clamped (no out-of-range access) and reported
+    as device error 2."""
+    q, k, v, g, beta, _ = _packed([400], 1, 128, 128)
+    stream = nat.stream_handle(q.device)
+    nat.lib().tileops_device_error_flag(stream, 1)
+    cu = torch.tensor([0, 300, 100, 400], dtype=torch.int32, device="cuda")
+    _run_varlen(q, k, v, g, beta, cu)
+    torch.cuda.synchronize()
+    assert nat.lib().tileops_device_error_flag(stream, 1) == 2
+    assert nat.lib().tileops_device_error_flag(stream, 0) == 0
+
+
+def test_rejects_bad_varlen_arguments():
+    q, k, v, g, beta = GdnPrefillWorkload(2, 64, 1, 128, 128).gen_inputs()
+    op = GatedDeltaNetPrefillFwdOp(2, 64, 1, 128, 128)
+    with pytest.raises(ValueError, match="batch size is expected to be 1"):
+        op(q, k, v, g, beta, cu_seqlens=_cu([64, 64]))
+    op1 = GatedDeltaNetPrefillFwdOp(1, 128, 1, 128, 128)
+    flat = lambda x: x.reshape(1, 128, *x.shape[2:])  # noqa: E731
+    args = (flat(q), flat(k), flat(v), flat(g), flat(beta))
+    with pytest.raises(ValueError, match="initial_state shape"):
+        op1(*args, torch.zeros(1, 1, 128, 128, device="cuda"), cu_seqlens=_cu([64, 64]))
+    with pytest.raises(ValueError, match="int32 or int64"):
+        op1(*args, cu_seqlens=_cu([64, 64]).float())

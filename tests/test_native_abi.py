@@ -92,6 +92,27 @@ def test_status_maps_to_python_exceptions():
         _native.call("tileops_no_such_entry")
 
 
+def test_gdn_varlen_workspace_and_validation():
+    lib = _native.lib()
+    per = (64 * 128 + 64 * 128 + 64 * 64) * 2 + (2 * 64 + 4) * 4
+    # (total / 64 + N) chunk slots per head, then the int32 slot table (16-byte rounded)
+    slots = 1000 // 64 + 3
+    assert lib.tileops_gdn_varlen_workspace_bytes(1000, 3, 2, 128, 128) == (
+        2 * slots * per + (slots * 4 + 15) // 16 * 16)
+    assert lib.tileops_gdn_varlen_workspace_bytes(64, 1, 1, 96, 128) == -1
+    assert lib.tileops_gdn_varlen_workspace_bytes(-1, 1, 1, 128, 128) == -1
+    fn = lib.tileops_gdn_prefill_varlen_fwd
+    head = [NULL] * 5 + [NULL]  # q, k, v, g, beta, cu_seqlens
+    tail = [NULL] * 4           # initial_state, o, final_state, workspace
+    # no sequences: nothing to do
+    assert fn(*head, 0, *tail, 0, 2, 128, 128, 64, 0.1, 2, NULL) == _native.OK
+    assert fn(*head, 2, *tail, 128, 2, 128, 128, 32, 0.1, 2, NULL) == _native.EBADSHAPE
+    assert fn(*head, 2, *tail, 128, 2, 128, 128, 64, 0.1, 1, NULL) == _native.EBADDTYPE
+    assert fn(*head, 2, *tail, 128, 2, 96, 128, 64, 0.1, 2, NULL) == _native.EBADSHAPE
+    assert fn(*head, -1, *tail, 128, 2, 128, 128, 64, 0.1, 2, NULL) == _native.EBADSHAPE
+    assert fn(*head, 2, *tail, 128, 2, 128, 128, 64, 0.1, 2, NULL) == _native.EINVAL
+
+
 def test_gdn_workspace_and_validation():
     lib = _native.lib()
     assert lib.tileops_gdn_workspace_bytes(4, 8192, 16, 128, 128) == 4 * 16 * 128 * (

@@ -123,3 +123,22 @@ def test_oracle_gdn_bthd_layout_matches_bhtd():
                                 m["scale"], i["state0"])
     torch.testing.assert_close(o.float(), t(case["outputs"]["o"]).to(o.dtype).float())
     torch.testing.assert_close(s, case["outputs"]["final_state"], atol=1e-6, rtol=1e-6)
+
+
+def test_oracle_gdn_varlen_matches_batched_golden():
+    """Packed sequences of equal length == the batched golden on the same tokens,
+    and an empty sequence passes its initial state through."""
+    case = load("gdn_b1_h2_t48_d16_dv16")
+    i, m = case["inputs"], case["meta"]
+    t = lambda a: a.transpose(1, 2).contiguous()  # noqa: E731  BHTD -> BTHD
+    q, k, v, g, beta = (t(i[n]) for n in ("q", "k", "v", "g", "beta"))
+    # two sequences of 24 tokens, an empty one between them
+    cu = torch.tensor([0, 24, 24, 48])
+    h0 = torch.cat([i["state0"], i["state0"] * 0.5, i["state0"] * 2.0], 0)
+    o, s = ref.gdn_prefill_varlen(q, k, v, g, beta, cu, m["scale"], h0)
+    split = lambda a: torch.cat([a[:, :24], a[:, 24:]], 0)  # noqa: E731
+    o_b, s_b = ref.gdn_prefill_bthd(split(q), split(k), split(v), split(g), split(beta),
+                                    m["scale"], torch.cat([h0[0:1], h0[2:3]], 0))
+    torch.testing.assert_close(o, torch.cat([o_b[0:1], o_b[1:2]], 1), atol=0, rtol=0)
+    torch.testing.assert_close(s[[0, 2]], s_b, atol=0, rtol=0)
+    torch.testing.assert_close(s[1], h0[1], atol=0, rtol=0)

@@ -9,6 +9,7 @@
 namespace tileops {
 
 constexpr int kErrMbarTimeout = 1;  // an mbarrier wait exceeded its poll limit
+constexpr int kErrBadSeqlens = 2;   // cu_seqlens not 0 = cu[0] <= ... <= cu[N] = total
 
 // Device address of the per-device error word (defined in capi.cu).  Kernels
 // receive it as an argument: each translation unit is a separate module, so

@@ -30,8 +30,22 @@
 // memory.
 //
 // Layout: q, k (B, T, H, dk) bf16; v, o (B, T, H, dv) bf16; g, beta (B, T, H)
-// fp32; initial / final state (B, H, dk, dv) fp32.  Tokens past T are
-// treated as k = v = q = 0, g = beta = 0 (they leave the state unchanged).
+// fp32; initial / final state (B, H, dk, dv) fp32.
+//
+// Sequences.  Both kernels see the tokens as rows: B sequences of T rows for
+// a uniform batch; for variable-length input one packed axis where sequence
+// n is rows [cu_seqlens[n], cu_seqlens[n+1]) (the fla varlen convention,
+// batch 1).  A chunk is 64 rows of one sequence; the rows of its last chunk
+// past the sequence end are padding: their g and beta read as 0 and their k,
+// q, v rows are zero (TMA zero fill past T for a uniform batch; for variable
+// length they hold the next sequence's tokens and are zeroed in shared memory
+// after the load), so they leave the state unchanged; their outputs are not
+// stored.  Chunk slots: sequence n with nc_n chunks owns the slots
+// [base_n, base_n + nc_n), base_n = n * nchunks for a uniform batch and
+// base_n = floor(cu[n] / 64) + n for variable length (disjoint ranges for a
+// non-decreasing cu, all below nslots = floor(total / 64) + N); chunk c of
+// head h is workspace unit H base_n + h nc_n + c (for a uniform batch the
+// (b, h, chunk) order, consecutive units = consecutive chunks of one head).
 #include <mutex>
 
 #include "common.cuh"
@@ -89,6 +103,66 @@ struct Ws {
   static constexpr int64_t kBytes = kHalfs * 2 + kTailFloats * 4;  // multiple of 16
 };
 
+// Where the sequences of one call lie on the flat token axis.
+struct SeqLayout {
+  const int* cu;         // nullptr: uniform batch; else N + 1 row offsets
+  const int* chunk_seq;  // variable length: the sequence whose slot range holds slot j
+  int rows;              // uniform: tokens per sequence; variable: total rows
+  int nchunks;           // uniform: chunks per sequence
+  int nslots;            // chunk slots per head
+};
+
+// TMA coordinates (row, batch) of row t of sequence n: the (D, H, T, B) map
+// of a uniform batch, the (D, H, total, 1) map of packed sequences.
+// kVar: packed sequences (sl.cu set); the kernels are instantiated for both
+// forms so a uniform batch carries none of the variable-length logic.
+template <bool kVar>
+__device__ __forceinline__ int2 map_row(int n, int bos, int t) {
+  if constexpr (kVar) return make_int2(t, 0);
+  else return make_int2(t - bos, n);
+}
+
+// Rows [bos, eos) of sequence n and its first chunk slot.  Variable-length
+// offsets are clamped into [0, rows] (and eos >= bos), so a malformed
+// cu_seqlens can give wrong numbers but never an out-of-range access; the
+// index kernel reports it.
+template <bool kVar>
+__device__ __forceinline__ void seq_span(const SeqLayout& sl, int n, int& bos, int& eos,
+                                         int& base) {
+  if constexpr (!kVar) {
+    bos = n * sl.rows;
+    eos = bos + sl.rows;
+    base = n * sl.nchunks;
+  } else {
+    bos = min(max(sl.cu[n], 0), sl.rows);
+    eos = min(max(sl.cu[n + 1], bos), sl.rows);
+    base = (bos >> 6) + n;
+  }
+}
+
+// Variable length: chunk_seq[j] = the largest n with base_n <= j (the
+// sequence whose slot range [base_n, base_n+1) holds slot j).  Threads n < N
+// also check the offsets (cu[0] = 0, cu[N] = rows, non-decreasing) and report
+// kErrBadSeqlens otherwise.
+__global__ void gdn_chunk_index(SeqLayout sl, int nseq, int* __restrict__ chunk_seq, int* err) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  const int* cu = sl.cu;
+  if (j < nseq) {
+    const bool bad = cu[j] > cu[j + 1] || (j == 0 && cu[0] != 0) ||
+                     (j == nseq - 1 && cu[nseq] != sl.rows);
+    if (bad) report_device_error(err, kErrBadSeqlens);
+  }
+  if (j >= sl.nslots) return;
+  int lo = 0, hi = nseq - 1;  // invariant: base_lo <= j (base_0 = 0)
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    const int bos = min(max(cu[mid], 0), sl.rows);
+    if ((bos >> 6) + mid <= j) lo = mid;
+    else hi = mid - 1;
+  }
+  chunk_seq[j] = lo;
+}
+
 // =========================================================== kernel 1
 // 128 threads (4 warps), one CTA per (b, h, chunk); four CTAs per SM.
 // K, Q, V arrive by TMA as 128-byte-swizzled [64][64] bf16 boxes (tokens
@@ -135,6 +209,18 @@ __device__ __forceinline__ void sfrag_b_nk(uint32_t (&b)[4], uint32_t base, int 
   ldsm4(b, base + swz(n0 + (lane & 7) + ((mat >> 1) << 3), k0 + ((mat & 1) << 3)));
 }
 
+// Zeroes rows first..63 of `boxes` swizzled [64][64] bf16 boxes (8 KB apart);
+// a row is 128 contiguous bytes whatever the swizzle.  Called by every thread
+// of the CTA (strided over blockDim.x).
+__device__ __forceinline__ void zero_rows(uint8_t* tile, int boxes, int first) {
+  const int per_box = (kC - first) * 8;  // 16-byte units
+  for (int i = threadIdx.x; i < boxes * per_box; i += blockDim.x) {
+    const int bx = i / per_box, rem = i - bx * per_box;
+    *reinterpret_cast<uint4*>(tile + bx * 8192 + (first + (rem >> 3)) * 128 + (rem & 7) * 16) =
+        make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+
 constexpr int kLdTf = 68;  // fp32 row stride of Tf (16-byte aligned rows)
 constexpr int kLdA = 65;   // fp32 row stride of As
 
@@ -152,18 +238,20 @@ struct PrepSmem {
   static constexpr int kKe = kBeta + kC * 4;
   static constexpr int kEgp = kKe + kC * 4;     // e^gc
   static constexpr int kEgm = kEgp + kC * 4;    // e^-gc, and the factor flag after it
-  static constexpr int kBar = kEgm + kC * 4 + 16;  // two mbarriers + abort flag
-  static constexpr int kBytes = kBar + 32;
+  // two mbarriers, the abort flag, then the chunk's (map row, map batch,
+  // head, first row to zero) read back late instead of held in registers
+  static constexpr int kBar = kEgm + kC * 4 + 16;
+  static constexpr int kBytes = kBar + 48;
   static constexpr int kAlloc = kBytes + 1024;  // room to align the base to 1 KB
 };
 
-template <int DK, int DV>
+template <int DK, int DV, bool kVar>
 __global__ void __launch_bounds__(128, 4)
     gdn_prepare(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                 const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_wk,
                 const __grid_constant__ CUtensorMap tm_u, const float* __restrict__ g,
-                const float* __restrict__ beta, __nv_bfloat16* __restrict__ ws, int T, int H,
-                int nchunks, float scale, int* err) {
+                const float* __restrict__ beta, __nv_bfloat16* __restrict__ ws, SeqLayout sl,
+                int H, float scale, int* err) {
   using L = PrepSmem<DK, DV>;
   using W = Ws<DK, DV>;
   extern __shared__ uint8_t smem_raw[];
@@ -181,13 +269,25 @@ __global__ void __launch_bounds__(128, 4)
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + L::kBar);       // K, Q
   uint64_t* bar_v = reinterpret_cast<uint64_t*>(sm + L::kBar + 8);  // V
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + L::kBar + 16);
+  int* chunk_info = reinterpret_cast<int*>(sm + L::kBar + 32);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g8 = lane >> 2, t2 = (lane & 3) * 2;
-  const int chunk = blockIdx.x % nchunks;
-  const int bh = blockIdx.x / nchunks;
-  const int b = bh / H, h = bh - (bh / H) * H;
-  const int t0 = chunk * kC;
+  // CTA = workspace unit u = H base_n + h nc_n + c.
+  const int u = blockIdx.x;
+  const int n = kVar ? sl.chunk_seq[u / H] : u / (H * sl.nchunks);
+  int bos, eos, base;
+  seq_span<kVar>(sl, n, bos, eos, base);
+  const int nc = kVar ? (eos - bos + kC - 1) / kC : sl.nchunks;
+  const int r = u - H * base;
+  if constexpr (kVar) {
+    if (r < 0 || r >= H * nc) return;  // a unit past the sequence's chunks
+  }
+  const int h = r / nc;
+  const int t0 = bos + (r - h * nc) * kC;  // first row of the chunk
+  const int nvalid = min(kC, eos - t0);   // rows of this sequence in it
+  const int zpad = kVar ? nvalid : kC;  // first row to zero after a load
+  const int2 mrow = map_row<kVar>(n, bos, t0);
   __nv_bfloat16* wsc = ws + static_cast<int64_t>(blockIdx.x) * (W::kBytes / 2);
   float* wsf = reinterpret_cast<float*>(wsc);
 
@@ -195,6 +295,10 @@ __global__ void __launch_bounds__(128, 4)
     sm100::mbar_init(bar, 1);
     sm100::mbar_init(bar_v, 1);
     *abort_flag = 0;
+    chunk_info[0] = mrow.x;
+    chunk_info[1] = mrow.y;
+    chunk_info[2] = h;
+    chunk_info[3] = zpad;
     sm100::fence_mbar_init();
   }
   __syncthreads();
@@ -202,21 +306,20 @@ __global__ void __launch_bounds__(128, 4)
     sm100::mbar_arrive_expect_tx(bar, 2 * DK * kC * 2);
 #pragma unroll
     for (int c = 0; c < DK / 64; ++c) {
-      sm100::tma_load_4d(sm + L::kKs + c * 8192, &tm_k, bar, c * 64, h, t0, b);
-      sm100::tma_load_4d(sm + L::kQs + c * 8192, &tm_q, bar, c * 64, h, t0, b);
+      sm100::tma_load_4d(sm + L::kKs + c * 8192, &tm_k, bar, c * 64, h, mrow.x, mrow.y);
+      sm100::tma_load_4d(sm + L::kQs + c * 8192, &tm_q, bar, c * 64, h, mrow.x, mrow.y);
     }
   }
   if (warp == 0) {
     // inclusive cumsum of g over the 64 tokens: two per lane + warp scan
     float g0 = 0.0f, g1 = 0.0f, b0 = 0.0f, b1 = 0.0f;
-    const int ta = t0 + 2 * lane, tb = ta + 1;
-    if (ta < T) {
-      const int64_t o = (static_cast<int64_t>(b) * T + ta) * H + h;
+    if (2 * lane < nvalid) {
+      const int64_t o = static_cast<int64_t>(t0 + 2 * lane) * H + h;
       g0 = g[o];
       b0 = beta[o];
     }
-    if (tb < T) {
-      const int64_t o = (static_cast<int64_t>(b) * T + tb) * H + h;
+    if (2 * lane + 1 < nvalid) {
+      const int64_t o = static_cast<int64_t>(t0 + 2 * lane + 1) * H + h;
       g1 = g[o];
       b1 = beta[o];
     }
@@ -253,6 +356,11 @@ __global__ void __launch_bounds__(128, 4)
     return;
   }
   const uint32_t sK = sb + L::kKs, sQ = sb + L::kQs, sV = sb + L::kVs;
+  if (zpad < kC) {  // padding rows of K and Q -> 0
+    zero_rows(sm + L::kKs, DK / 64, zpad);
+    zero_rows(sm + L::kQs, DK / 64, zpad);
+    __syncthreads();
+  }
 
   // ---- KK^T -> A (strictly lower, fp32) and QK^T -> QKm (lower, bf16, to the
   // workspace); warp w owns rows 16w..16w+15 and only needs columns <= them.
@@ -394,7 +502,8 @@ __global__ void __launch_bounds__(128, 4)
     sm100::mbar_arrive_expect_tx(bar_v, DV * kC * 2);
 #pragma unroll
     for (int c = 0; c < DV / 64; ++c)
-      sm100::tma_load_4d(sm + L::kVs + c * 8192, &tm_v, bar_v, c * 64, h, t0, b);
+      sm100::tma_load_4d(sm + L::kVs + c * 8192, &tm_v, bar_v, c * 64, chunk_info[2],
+                         chunk_info[0], chunk_info[1]);
   }
 
   // ---- Tk = T diag(beta e^gc), Tv = T diag(beta) in bf16, swizzled [64][64]
@@ -448,6 +557,10 @@ __global__ void __launch_bounds__(128, 4)
           }
           __syncthreads();
           return;
+        }
+        if (chunk_info[3] < kC) {  // padding rows of V -> 0
+          zero_rows(sm + L::kVs, DV / 64, chunk_info[3]);
+          __syncthreads();
         }
       }
       constexpr int kMaxD = DK > DV ? DK : DV;
@@ -533,13 +646,13 @@ struct ScanSmem {
   static constexpr int kAlloc = kBytes + 1024;
 };
 
-template <int DK, int DV>
+template <int DK, int DV, bool kVar>
 __global__ void __launch_bounds__(256, 1)
     gdn_scan(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
              const __grid_constant__ CUtensorMap tm_wk, const __grid_constant__ CUtensorMap tm_u,
              const __grid_constant__ CUtensorMap tm_qk, const __nv_bfloat16* __restrict__ ws,
              const float* __restrict__ h0, __nv_bfloat16* __restrict__ o, float* __restrict__ hT,
-             int T, int H, int nchunks, int* err) {
+             SeqLayout sl, int H, int* err) {
   using L = ScanSmem<DK>;
   using W = Ws<DK, DV>;
   extern __shared__ uint8_t smem_raw[];
@@ -550,21 +663,25 @@ __global__ void __launch_bounds__(256, 1)
   constexpr int kSlices = DV / kSlice;
   const int slice = blockIdx.x % kSlices;
   const int bh = blockIdx.x / kSlices;
-  const int b = bh / H, h = bh - (bh / H) * H;
+  const int b = bh / H, h = bh - (bh / H) * H;  // b: the sequence
   const int v0 = slice * kSlice;
   const int g8 = lane >> 2, t2 = (lane & 3) * 2;
+  int bos, eos, base;
+  seq_span<kVar>(sl, b, bos, eos, base);
+  const int nchunks = kVar ? (eos - bos + kC - 1) / kC : sl.nchunks;
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + L::kBar);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + L::kBar + 16);
 
   auto issue = [&](int s, int chunk) {  // thread 0 only
-    const int t0 = chunk * kC;
-    const int unit = bh * nchunks + chunk;  // workspace chunk index
+    const int t0 = bos + chunk * kC;
+    const int unit = H * base + h * nchunks + chunk;  // workspace chunk unit
+    const int2 mrow = map_row<kVar>(b, bos, t0);
     uint8_t* st = sm + s * L::kStage;
     sm100::mbar_arrive_expect_tx(&full[s], L::kLoadBytes);
 #pragma unroll
     for (int c = 0; c < DK / 64; ++c) {
-      sm100::tma_load_4d(st + L::kQs + c * 8192, &tm_q, &full[s], c * 64, h, t0, b);
-      sm100::tma_load_4d(st + L::kKs + c * 8192, &tm_k, &full[s], c * 64, h, t0, b);
+      sm100::tma_load_4d(st + L::kQs + c * 8192, &tm_q, &full[s], c * 64, h, mrow.x, mrow.y);
+      sm100::tma_load_4d(st + L::kKs + c * 8192, &tm_k, &full[s], c * 64, h, mrow.x, mrow.y);
       sm100::tma_load_3d(st + L::kWks + c * 8192, &tm_wk, &full[s], c * 64, 0, unit);
     }
     sm100::tma_load_3d(st + L::kUs, &tm_u, &full[s], v0, 0, unit);
@@ -586,7 +703,7 @@ __global__ void __launch_bounds__(256, 1)
     sm100::fence_mbar_init();
   }
   __syncthreads();
-  if (tid == 0) issue(0, 0);
+  if (tid == 0 && nchunks > 0) issue(0, 0);
 
   // State: warp w owns rows 16w..16w+15 of S (DK = 128: rows 0..127) as
   // 8 n-tiles of 16 x 8 accumulators (the 64-column slice).
@@ -628,6 +745,12 @@ __global__ void __launch_bounds__(256, 1)
     if (!__syncthreads_and(landed)) {  // also: the published state is visible
       failed_at = chunk;
       break;
+    }
+    const int nvalid = min(kC, eos - (bos + chunk * kC));
+    if (kVar && nvalid < kC) {  // padding rows of K -> 0 (they enter K^T err)
+      zero_rows(sm + s * L::kStage + L::kKs, DK / 64, nvalid);
+      sm100::fence_proxy_async_smem();  // before the stage's next TMA refill
+      __syncthreads();
     }
     const uint32_t st = sb + s * L::kStage;
     const uint32_t sQ = st + L::kQs, sK = st + L::kKs, sW = st + L::kWks;
@@ -689,17 +812,16 @@ __global__ void __launch_bounds__(256, 1)
       }
     }
     {
-      const int t0 = chunk * kC;
+      const int t0 = bos + chunk * kC;
 #pragma unroll
       for (int n = 0; n < 4; ++n)
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
           const int l = om0 + g8 + half * 8, c = on0 + n * 8 + t2;
-          const int t = t0 + l;
-          if (t < T)
-            *reinterpret_cast<uint32_t*>(o + ((static_cast<int64_t>(b) * T + t) * H + h) * DV +
-                                         v0 + c) = pack_bf16(o_acc[n][half * 2],
-                                                             o_acc[n][half * 2 + 1]);
+          if (l < nvalid)
+            *reinterpret_cast<uint32_t*>(o + (static_cast<int64_t>(t0 + l) * H + h) * DV + v0 +
+                                         c) = pack_bf16(o_acc[n][half * 2],
+                                                        o_acc[n][half * 2 + 1]);
         }
     }
     // S = e^gc_last S + K^T (decayed err)
@@ -802,14 +924,14 @@ constexpr int kScanTcMath = 256;
 constexpr int kScanTcThreads = kScanTcMath + 64;
 constexpr uint32_t kScanTcCols = 512;
 
-template <int DV>
+template <int DV, bool kVar>
 __global__ void __launch_bounds__(kScanTcThreads, 1)
     gdn_scan_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                 const __grid_constant__ CUtensorMap tm_wk,
                 const __grid_constant__ CUtensorMap tm_u,
                 const __grid_constant__ CUtensorMap tm_qk, const __nv_bfloat16* __restrict__ ws,
                 const float* __restrict__ h0, __nv_bfloat16* __restrict__ o,
-                float* __restrict__ hT, int T, int H, int nchunks, int* err) {
+                float* __restrict__ hT, SeqLayout sl, int H, int* err) {
   using namespace sm100;
   using L = ScanTcSmem;
   using W = Ws<128, DV>;
@@ -823,8 +945,20 @@ __global__ void __launch_bounds__(kScanTcThreads, 1)
   constexpr int kSlices = DV / kSlice;
   const int slice = blockIdx.x % kSlices;
   const int bh = blockIdx.x / kSlices;
-  const int b = bh / H, h = bh - (bh / H) * H;
+  const int b = bh / H, h = bh - (bh / H) * H;  // b: the sequence
   const int v0 = slice * kSlice;
+  int bos, eos, base;
+  seq_span<kVar>(sl, b, bos, eos, base);
+  const int nchunks = kVar ? (eos - bos + kC - 1) / kC : sl.nchunks;
+  if (kVar && nchunks == 0) {  // an empty sequence: the final state is the initial one
+    if (hT != nullptr)
+      for (int i = tid; i < DK * kSlice; i += blockDim.x) {
+        const int64_t at = ((static_cast<int64_t>(b) * H + h) * DK + i / kSlice) * DV + v0 +
+                           i % kSlice;
+        hT[at] = h0 ? h0[at] : 0.0f;
+      }
+    return;
+  }
 
   if (tid == 0) {
     for (int s = 0; s < kTcStages; ++s) {
@@ -879,14 +1013,16 @@ __global__ void __launch_bounds__(kScanTcThreads, 1)
         const int use = c / kTcStages;
         if (use > 0 && !mbar_wait(&bars->empty[s], (use - 1) & 1, err, abort_flag)) break;
         uint8_t* st = sm + s * L::kStage;
-        const int t0 = c * kC;
-        const int unit = bh * nchunks + c;
+        const int t0 = bos + c * kC;
+        const int unit = H * base + h * nchunks + c;
+        const int2 mrow = map_row<kVar>(b, bos, t0);
         mbar_arrive_expect_tx(&bars->full[s], L::kLoadBytes);
 #pragma unroll
         for (int k = 0; k < DK / 64; ++k) {
           tma_load_3d(st + L::kA1 + k * 16384, &tm_wk, &bars->full[s], k * 64, 0, unit);
-          tma_load_4d(st + L::kA1 + k * 16384 + 8192, &tm_q, &bars->full[s], k * 64, h, t0, b);
-          tma_load_4d(st + L::kK + k * 8192, &tm_k, &bars->full[s], k * 64, h, t0, b);
+          tma_load_4d(st + L::kA1 + k * 16384 + 8192, &tm_q, &bars->full[s], k * 64, h, mrow.x,
+                      mrow.y);
+          tma_load_4d(st + L::kK + k * 8192, &tm_k, &bars->full[s], k * 64, h, mrow.x, mrow.y);
         }
         tma_load_3d(st + L::kUQ, &tm_u, &bars->full[s], v0, 0, unit);
         tma_load_3d(st + L::kUQ + 8192, &tm_qk, &bars->full[s], 0, 0, unit);
@@ -997,6 +1133,9 @@ __global__ void __launch_bounds__(kScanTcThreads, 1)
     for (int c = 0; ok && c < nchunks; ++c) {
       const int s = c % kTcStages;
       const float* tail = reinterpret_cast<const float*>(sm + L::kTail + s * L::kTailBytes);
+      const int t0 = bos + c * kC;
+      const int nvalid = min(kC, eos - t0);
+      const int zpad = kVar ? nvalid : kC;  // padding rows to zero
       float qsc = 0.0f;
       if (err_rows) {
         // err = U - Wk S for token l (D1 rows 0-63) -> Es, Ed rows l.
@@ -1020,6 +1159,14 @@ __global__ void __launch_bounds__(kScanTcThreads, 1)
           }
           *reinterpret_cast<uint4*>(Es + swz(l, cb + 8 * u)) = pe;
           *reinterpret_cast<uint4*>(Ed + swz(l, cb + 8 * u)) = pd;
+        }
+        if (l >= zpad) {
+          // A padding row of packed sequences: its K row (box cb / 32 of the K tile) -> 0 before
+          // MMA3 reads it (this thread waited for the stage in `publish`).
+          uint4* krow = reinterpret_cast<uint4*>(sm + s * L::kStage + L::kK + (cb >> 5) * 8192 +
+                                                 l * 128);
+#pragma unroll
+          for (int u = 0; u < 8; ++u) krow[u] = make_uint4(0u, 0u, 0u, 0u);
         }
         fence_proxy_async_smem();
       } else {
@@ -1057,10 +1204,9 @@ __global__ void __launch_bounds__(kScanTcThreads, 1)
         tmem_ld32(t_d2(c) + lane_off + cb, y);
         tmem_wait_ld_regs(x);
         tmem_wait_ld_regs(y);
-        const int t = c * kC + l;
-        if (t < T) {
+        if (l < nvalid) {
           uint4* orow = reinterpret_cast<uint4*>(
-              o + ((static_cast<int64_t>(b) * T + t) * H + h) * DV + v0 + cb);
+              o + (static_cast<int64_t>(t0 + l) * H + h) * DV + v0 + cb);
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             uint4 pk;
@@ -1085,21 +1231,25 @@ __global__ void __launch_bounds__(kScanTcThreads, 1)
   }
 }
 
-template <int DK, int DV>
+// nseq sequences; `sl` says where they lie.  The q / k / v maps are (D, H,
+// map_rows, map_batch): (T, B) for a uniform batch, (total, 1) for packed
+// sequences.  For variable length, sl.chunk_seq points at nslots ints the
+// index kernel fills first.
+template <int DK, int DV, bool kVar>
 int launch_gdn(const void* q, const void* k, const void* v, const float* g, const float* beta,
-               const float* h0, void* o, float* hT, void* ws, int B, int T, int H, float scale,
-               cudaStream_t s) {
-  const int nchunks = (T + kC - 1) / kC;
-  auto k1 = gdn_prepare<DK, DV>;
-  auto k2 = gdn_scan<DK, DV>;
+               const float* h0, void* o, float* hT, void* ws, SeqLayout sl, int nseq,
+               int map_rows, int map_batch, int H, float scale, cudaStream_t s) {
+  auto k1 = gdn_prepare<DK, DV, kVar>;
+  auto k2 = gdn_scan<DK, DV, kVar>;
   CUtensorMap tq, tk, tv;
-  if (!make_bshd_map(&tq, q, DK, H, T, B, kC, true) || !make_bshd_map(&tk, k, DK, H, T, B, kC, true) ||
-      !make_bshd_map(&tv, v, DV, H, T, B, kC, true))
+  if (!make_bshd_map(&tq, q, DK, H, map_rows, map_batch, kC, true) ||
+      !make_bshd_map(&tk, k, DK, H, map_rows, map_batch, kC, true) ||
+      !make_bshd_map(&tv, v, DV, H, map_rows, map_batch, kC, true))
     return TILEOPS_ELAUNCH;
   const int smem1 = PrepSmem<DK, DV>::kAlloc;
   const int smem2 = ScanSmem<DK>::kAlloc;
   // Workspace tiles as 3-D maps (columns, 64 rows, chunk units).
-  const uint64_t units = static_cast<uint64_t>(B) * H * nchunks;
+  const uint64_t units = static_cast<uint64_t>(H) * sl.nslots;
   const uint64_t wb = Ws<DK, DV>::kBytes;
   CUtensorMap twk, tu, tqk;
   {
@@ -1117,31 +1267,70 @@ int launch_gdn(const void* q, const void* k, const void* v, const float* g, cons
           cudaSuccess ||
       cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, smem2) != cudaSuccess)
     return TILEOPS_ELAUNCH;
-  const int64_t grid1 = static_cast<int64_t>(B) * H * nchunks;
-  if (grid1 > 0x7fffffffLL) return TILEOPS_EBADSHAPE;
-  k1<<<static_cast<unsigned>(grid1), 128, smem1, s>>>(
-      tq, tk, tv, twk, tu, g, beta, static_cast<__nv_bfloat16*>(ws), T, H, nchunks, scale,
+  if (units > 0x7fffffffULL) return TILEOPS_EBADSHAPE;
+  if constexpr (kVar) {
+    gdn_chunk_index<<<(sl.nslots + 255) / 256, 256, 0, s>>>(sl, nseq,
+                                                            const_cast<int*>(sl.chunk_seq),
+                                                            device_error_ptr());
+    const int st = launch_status();
+    if (st != TILEOPS_OK) return st;
+  }
+  k1<<<static_cast<unsigned>(units), 128, smem1, s>>>(
+      tq, tk, tv, twk, tu, g, beta, static_cast<__nv_bfloat16*>(ws), sl, H, scale,
       device_error_ptr());
   int st = launch_status();
   if (st != TILEOPS_OK) return st;
+  const unsigned grid2 = static_cast<unsigned>(nseq * H * (DV / kSlice));
   if constexpr (DK == 128) {
     // dk = 128: the tensor-core (tcgen05) scan; its final-state stores are
     // 16-byte vectors, so it needs an aligned final_state.
     if (hT == nullptr || aligned16(hT)) {
-      auto k3 = gdn_scan_tc<DV>;
+      auto k3 = gdn_scan_tc<DV, kVar>;
       if (cudaFuncSetAttribute(k3, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                ScanTcSmem::kAlloc) != cudaSuccess)
         return TILEOPS_ELAUNCH;
-      k3<<<static_cast<unsigned>(B * H * (DV / kSlice)), kScanTcThreads, ScanTcSmem::kAlloc, s>>>(
+      k3<<<grid2, kScanTcThreads, ScanTcSmem::kAlloc, s>>>(
           tq, tk, twk, tu, tqk, static_cast<const __nv_bfloat16*>(ws), h0,
-          static_cast<__nv_bfloat16*>(o), hT, T, H, nchunks, device_error_ptr());
+          static_cast<__nv_bfloat16*>(o), hT, sl, H, device_error_ptr());
       return launch_status();
     }
   }
-  k2<<<static_cast<unsigned>(B * H * (DV / kSlice)), 256, smem2, s>>>(
-      tq, tk, twk, tu, tqk, static_cast<const __nv_bfloat16*>(ws), h0,
-      static_cast<__nv_bfloat16*>(o), hT, T, H, nchunks, device_error_ptr());
+  k2<<<grid2, 256, smem2, s>>>(tq, tk, twk, tu, tqk, static_cast<const __nv_bfloat16*>(ws), h0,
+                               static_cast<__nv_bfloat16*>(o), hT, sl, H, device_error_ptr());
   return launch_status();
+}
+
+int64_t ws_bytes_per_chunk(int64_t dim_k, int64_t dim_v) {
+  if (dim_k == 128 && dim_v == 128) return Ws<128, 128>::kBytes;
+  if (dim_k == 64 && dim_v == 64) return Ws<64, 64>::kBytes;
+  if (dim_k == 128 && dim_v == 64) return Ws<128, 64>::kBytes;
+  if (dim_k == 64 && dim_v == 128) return Ws<64, 128>::kBytes;
+  return -1;
+}
+
+// Variable length: chunk slots per head, and where the chunk -> sequence
+// table sits in the workspace (after the chunk units, 16-byte aligned).
+int64_t varlen_slots(int64_t total_len, int64_t num_seqs) { return total_len / kC + num_seqs; }
+int64_t varlen_table_offset(int64_t total_len, int64_t num_seqs, int64_t heads, int64_t per) {
+  return heads * varlen_slots(total_len, num_seqs) * per;
+}
+
+template <bool kVar>
+int dispatch_gdn(const void* q, const void* k, const void* v, const float* g, const float* beta,
+                 const float* h0, void* o, float* hT, void* ws, SeqLayout sl, int nseq,
+                 int map_rows, int map_batch, int H, int dim_k, int dim_v, float scale,
+                 cudaStream_t s) {
+  if (dim_k == 128 && dim_v == 128)
+    return launch_gdn<128, 128, kVar>(q, k, v, g, beta, h0, o, hT, ws, sl, nseq, map_rows, map_batch,
+                                H, scale, s);
+  if (dim_k == 64 && dim_v == 64)
+    return launch_gdn<64, 64, kVar>(q, k, v, g, beta, h0, o, hT, ws, sl, nseq, map_rows, map_batch, H,
+                              scale, s);
+  if (dim_k == 128 && dim_v == 64)
+    return launch_gdn<128, 64, kVar>(q, k, v, g, beta, h0, o, hT, ws, sl, nseq, map_rows, map_batch,
+                               H, scale, s);
+  return launch_gdn<64, 128, kVar>(q, k, v, g, beta, h0, o, hT, ws, sl, nseq, map_rows, map_batch, H,
+                             scale, s);
 }
 
 }  // namespace
@@ -1153,12 +1342,8 @@ extern "C" int64_t tileops_gdn_workspace_bytes(int64_t batch, int64_t seq_len, i
                                                int64_t dim_k, int64_t dim_v) {
   if (batch < 0 || seq_len < 0 || heads <= 0) return -1;
   const int64_t nchunks = (seq_len + kC - 1) / kC;
-  int64_t per = 0;
-  if (dim_k == 128 && dim_v == 128) per = Ws<128, 128>::kBytes;
-  else if (dim_k == 64 && dim_v == 64) per = Ws<64, 64>::kBytes;
-  else if (dim_k == 128 && dim_v == 64) per = Ws<128, 64>::kBytes;
-  else if (dim_k == 64 && dim_v == 128) per = Ws<64, 128>::kBytes;
-  else return -1;
+  const int64_t per = ws_bytes_per_chunk(dim_k, dim_v);
+  if (per < 0) return -1;
   return batch * heads * nchunks * per;
 }
 
@@ -1170,29 +1355,73 @@ extern "C" int tileops_gdn_prefill_fwd(const void* q, const void* k, const void*
                                        int64_t dim_v, int64_t chunk_size, double scale,
                                        int dtype, void* stream) {
   if (batch < 0 || seq_len < 0 || heads <= 0 || batch * heads > (1 << 24) ||
-      seq_len > (1 << 30))
+      seq_len > (1 << 30) || batch * seq_len > 0x7fffffffLL)
     return TILEOPS_EBADSHAPE;
   if (chunk_size != kC) return TILEOPS_EBADSHAPE;
-  if (!((dim_k == 64 || dim_k == 128) && (dim_v == 64 || dim_v == 128))) return TILEOPS_EBADSHAPE;
+  if (ws_bytes_per_chunk(dim_k, dim_v) < 0) return TILEOPS_EBADSHAPE;
   if (dtype != TILEOPS_DT_BF16) return TILEOPS_EBADDTYPE;
   if (batch == 0 || seq_len == 0) return TILEOPS_OK;
   if (!q || !k || !v || !g || !beta || !o || !workspace) return TILEOPS_EINVAL;
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || !aligned16(workspace))
     return TILEOPS_EALIGN;
+  const int B = static_cast<int>(batch), T = static_cast<int>(seq_len);
+  const int nchunks = (T + kC - 1) / kC;
+  const SeqLayout sl{nullptr, nullptr, T, nchunks, B * nchunks};
+  return dispatch_gdn<false>(q, k, v, g, beta, initial_state, o, final_state, workspace, sl, B, T,
+                             B,
+                      static_cast<int>(heads), static_cast<int>(dim_k), static_cast<int>(dim_v),
+                      static_cast<float>(scale), as_stream(stream));
+}
+
+extern "C" int64_t tileops_gdn_varlen_workspace_bytes(int64_t total_len, int64_t num_seqs,
+                                                      int64_t heads, int64_t dim_k,
+                                                      int64_t dim_v) {
+  if (total_len < 0 || num_seqs < 0 || heads <= 0) return -1;
+  const int64_t per = ws_bytes_per_chunk(dim_k, dim_v);
+  if (per < 0) return -1;
+  const int64_t table = (varlen_slots(total_len, num_seqs) * 4 + 15) / 16 * 16;
+  return varlen_table_offset(total_len, num_seqs, heads, per) + table;
+}
+
+extern "C" int tileops_gdn_prefill_varlen_fwd(const void* q, const void* k, const void* v,
+                                              const float* g, const float* beta,
+                                              const int32_t* cu_seqlens, int64_t num_seqs,
+                                              const float* initial_state, void* o,
+                                              float* final_state, void* workspace,
+                                              int64_t total_len, int64_t heads, int64_t dim_k,
+                                              int64_t dim_v, int64_t chunk_size, double scale,
+                                              int dtype, void* stream) {
+  if (total_len < 0 || num_seqs < 0 || heads <= 0 || total_len > (1 << 30) ||
+      num_seqs > (1 << 24) || heads * varlen_slots(total_len, num_seqs) > 0x7fffffffLL ||
+      num_seqs * heads > (1 << 24))
+    return TILEOPS_EBADSHAPE;
+  if (chunk_size != kC) return TILEOPS_EBADSHAPE;
+  const int64_t per = ws_bytes_per_chunk(dim_k, dim_v);
+  if (per < 0) return TILEOPS_EBADSHAPE;
+  if (dtype != TILEOPS_DT_BF16) return TILEOPS_EBADDTYPE;
+  if (num_seqs == 0) return TILEOPS_OK;
   cudaStream_t s = as_stream(stream);
-  const int B = static_cast<int>(batch), T = static_cast<int>(seq_len), H = static_cast<int>(heads);
-  const float sc = static_cast<float>(scale);
-  if (dim_k == 128 && dim_v == 128)
-    return launch_gdn<128, 128>(q, k, v, g, beta, initial_state, o, final_state, workspace, B, T,
-                                H, sc, s);
-  if (dim_k == 64 && dim_v == 64)
-    return launch_gdn<64, 64>(q, k, v, g, beta, initial_state, o, final_state, workspace, B, T, H,
-                              sc, s);
-  if (dim_k == 128 && dim_v == 64)
-    return launch_gdn<128, 64>(q, k, v, g, beta, initial_state, o, final_state, workspace, B, T,
-                               H, sc, s);
-  return launch_gdn<64, 128>(q, k, v, g, beta, initial_state, o, final_state, workspace, B, T, H,
-                             sc, s);
+  const int64_t state_bytes = num_seqs * heads * dim_k * dim_v * 4;
+  if (total_len == 0) {  // every sequence is empty: final state = initial state
+    if (!final_state) return TILEOPS_OK;
+    const cudaError_t e =
+        initial_state ? cudaMemcpyAsync(final_state, initial_state, state_bytes,
+                                        cudaMemcpyDeviceToDevice, s)
+                      : cudaMemsetAsync(final_state, 0, state_bytes, s);
+    return e == cudaSuccess ? TILEOPS_OK : TILEOPS_ELAUNCH;
+  }
+  if (!q || !k || !v || !g || !beta || !o || !workspace || !cu_seqlens) return TILEOPS_EINVAL;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || !aligned16(workspace))
+    return TILEOPS_EALIGN;
+  const int64_t nslots = varlen_slots(total_len, num_seqs);
+  auto* table = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) +
+                                       varlen_table_offset(total_len, num_seqs, heads, per));
+  const SeqLayout sl{cu_seqlens, table, static_cast<int>(total_len), 0,
+                     static_cast<int>(nslots)};
+  return dispatch_gdn<true>(q, k, v, g, beta, initial_state, o, final_state, workspace, sl,
+                      static_cast<int>(num_seqs), static_cast<int>(total_len), 1,
+                      static_cast<int>(heads), static_cast<int>(dim_k), static_cast<int>(dim_v),
+                      static_cast<float>(scale), s);
 }
 
 // ------------------------------------------------------------------------

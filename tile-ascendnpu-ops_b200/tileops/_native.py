@@ -78,6 +78,8 @@ _SIGNATURES: dict[str, list] = {
     "tileops_gdn_prefill_fwd": [_p] * 9 + [_i64] * 6 + [_d, _i, _p],
     "tileops_gdn_workspace_bytes": [_i64] * 5,
     "tileops_gdn_prefill_fwd_noalloc": [_p] * 8 + [_i64] * 6 + [_d, _i, _p],
+    "tileops_gdn_varlen_workspace_bytes": [_i64] * 5,
+    "tileops_gdn_prefill_varlen_fwd": [_p] * 6 + [_i64] + [_p] * 4 + [_i64] * 5 + [_d, _i, _p],
     "tileops_device_error_flag": [_p, _i],
     "tileops_abi_version": [],
     "tileops_status_string": [_i],
@@ -116,6 +118,7 @@ def lib() -> ctypes.CDLL:
                 fn.restype = {
                     "tileops_status_string": ctypes.c_char_p,
                     "tileops_gdn_workspace_bytes": ctypes.c_int64,
+                    "tileops_gdn_varlen_workspace_bytes": ctypes.c_int64,
                 }.get(name, ctypes.c_int)
             _lib = handle
     return _lib

@@ -1,14 +1,17 @@
 """GDNPrefillFwdKernel: gated delta rule, chunked prefill.
 
-Native entry point ``tileops_gdn_prefill_fwd`` (two kernels: a chunk-parallel
-prepare kernel computing the WY factors of every 64-token chunk on tensor
-cores, then a scan over chunks per (batch, head, 64-column slice of the value
-dimension) with the state in fp32 registers).  The reference has no kernel
-for this op; its probe kernel is examples/gdn_prefill/probe/gdn_prefill_probe.py:83
+Native entry points ``tileops_gdn_prefill_fwd`` and, for packed
+variable-length input (``cu_seqlens``), ``tileops_gdn_prefill_varlen_fwd``.
+Two kernels: a chunk-parallel prepare kernel computing the WY factors of every
+64-token chunk on tensor cores, then a scan over the chunks of each (sequence,
+head, 64-column slice of the value dimension), the state in TMEM (tcgen05,
+dk = 128) or in fp32 registers (dk = 64).  The reference has no kernel for
+this op; its probe kernel is examples/gdn_prefill/probe/gdn_prefill_probe.py:83
 and the semantics are its sequential golden at :60-77.
 
 The scratch workspace (per-chunk WY factors) is allocated here through the
-torch caching allocator, sized by ``tileops_gdn_workspace_bytes``.
+torch caching allocator, sized by ``tileops_gdn_workspace_bytes`` /
+``tileops_gdn_varlen_workspace_bytes``.
 """
 
 from __future__ import annotations
@@ -60,7 +63,15 @@ class GDNPrefillFwdKernel(Kernel):
             raise ValueError("unsupported GDN shape")
         return int(n)
 
-    def forward(self, q, k, v, g, beta, initial_state=None, output_final_state: bool = True):
+    def varlen_workspace_bytes(self, num_seqs: int) -> int:
+        n = _native.lib().tileops_gdn_varlen_workspace_bytes(
+            self.batch * self.seq_len, num_seqs, self.heads, self.dim_k, self.dim_v)
+        if n < 0:
+            raise ValueError("unsupported GDN shape")
+        return int(n)
+
+    def forward(self, q, k, v, g, beta, initial_state=None, output_final_state: bool = True,
+                cu_seqlens=None):
         q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
         g = g.contiguous().float()
         beta = beta.contiguous().float()
@@ -68,15 +79,32 @@ class GDNPrefillFwdKernel(Kernel):
             initial_state = initial_state.contiguous().float()
         o = torch.empty((self.batch, self.seq_len, self.heads, self.dim_v), dtype=self.dtype,
                         device=q.device)
-        final = (torch.empty((self.batch, self.heads, self.dim_k, self.dim_v),
+        # One state per sequence: the batch rows, or the packed sequences.
+        nseq = self.batch if cu_seqlens is None else cu_seqlens.numel() - 1
+        final = (torch.empty((nseq, self.heads, self.dim_k, self.dim_v),
                              dtype=torch.float32, device=q.device)
                  if output_final_state else None)
-        ws = torch.empty(max(self.workspace_bytes(), 16), dtype=torch.uint8, device=q.device)
+        if cu_seqlens is None:
+            ws = torch.empty(max(self.workspace_bytes(), 16), dtype=torch.uint8,
+                             device=q.device)
+            _native.launch(
+                "tileops_gdn_prefill_fwd", q.device,
+                _native.ptr(q), _native.ptr(k), _native.ptr(v), _native.ptr(g),
+                _native.ptr(beta), _native.ptr(initial_state), _native.ptr(o),
+                _native.ptr(final), _native.ptr(ws),
+                self.batch, self.seq_len, self.heads, self.dim_k, self.dim_v, self.chunk_size,
+                float(self.scale), _native.dtype_code(self.dtype),
+            )
+            return o, final
+        cu = cu_seqlens.to(device=q.device, dtype=torch.int32).contiguous()
+        ws = torch.empty(max(self.varlen_workspace_bytes(nseq), 16), dtype=torch.uint8,
+                         device=q.device)
         _native.launch(
-            "tileops_gdn_prefill_fwd", q.device,
+            "tileops_gdn_prefill_varlen_fwd", q.device,
             _native.ptr(q), _native.ptr(k), _native.ptr(v), _native.ptr(g), _native.ptr(beta),
-            _native.ptr(initial_state), _native.ptr(o), _native.ptr(final), _native.ptr(ws),
-            self.batch, self.seq_len, self.heads, self.dim_k, self.dim_v, self.chunk_size,
+            _native.ptr(cu), nseq, _native.ptr(initial_state), _native.ptr(o),
+            _native.ptr(final), _native.ptr(ws),
+            self.batch * self.seq_len, self.heads, self.dim_k, self.dim_v, self.chunk_size,
             float(self.scale), _native.dtype_code(self.dtype),
         )
         return o, final

@@ -9,13 +9,18 @@ API in the style of the other ops:
 
     GatedDeltaNetPrefillFwdOp(batch, seq_len, heads, dim_k, dim_v, chunk_size=64,
                               scale=None, dtype=torch.bfloat16, kernel_map=None)
-    forward(q, k, v, g, beta, initial_state=None) -> (o, final_state)
+    forward(q, k, v, g, beta, initial_state=None, cu_seqlens=None) -> (o, final_state)
 
 Layout BTHD (the fla convention): q, k (B, T, H, dk), v (B, T, H, dv) bf16; g
 (B, T, H) fp32 per-token log decay (<= 0 for decay); beta (B, T, H) fp32;
 initial_state (B, H, dk, dv) fp32 or None (zeros).  Returns o (B, T, H, dv)
 bf16 and the final state (B, H, dk, dv) fp32; passing it as the next call's
 initial_state continues the sequence (chunked prefill of long contexts).
+
+Variable-length input follows fla's ``cu_seqlens`` convention: batch 1, the N
+sequences packed along the token axis, ``cu_seqlens`` an integer device tensor
+of N + 1 offsets (0, ..., T); initial_state and the final state are then
+(N, H, dk, dv), one per sequence.
 """
 
 from __future__ import annotations
@@ -61,10 +66,11 @@ class GatedDeltaNetPrefillFwdOp(Op):
         return {"gdn_prefill": GDNPrefillFwdKernel}
 
     def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor,
-                beta: torch.Tensor, initial_state: Optional[torch.Tensor] = None):
+                beta: torch.Tensor, initial_state: Optional[torch.Tensor] = None,
+                cu_seqlens: Optional[torch.Tensor] = None):
         backend = get_device_backend()
         for name, t in (("q", q), ("k", k), ("v", v), ("g", g), ("beta", beta),
-                        ("initial_state", initial_state)):
+                        ("initial_state", initial_state), ("cu_seqlens", cu_seqlens)):
             if t is not None and not backend.is_device_tensor(t):
                 raise ValueError(f"{name} must be a {backend.name} tensor, got device {t.device}")
         B, T, H, dk, dv = self.batch, self.seq_len, self.heads, self.dim_k, self.dim_v
@@ -76,10 +82,22 @@ class GatedDeltaNetPrefillFwdOp(Op):
         for name, t in (("q", q), ("k", k), ("v", v)):
             if t.dtype != self.dtype:
                 raise ValueError(f"Expected {name}.dtype {self.dtype}, got {t.dtype}")
-        if initial_state is not None and tuple(initial_state.shape) != (B, H, dk, dv):
-            raise ValueError(f"Expected initial_state shape {(B, H, dk, dv)}, "
+        nseq = B
+        if cu_seqlens is not None:
+            if B != 1:
+                raise ValueError(f"The batch size is expected to be 1 rather than {B} when "
+                                 "using `cu_seqlens`. Please flatten variable-length inputs "
+                                 "before processing.")
+            if cu_seqlens.dim() != 1 or cu_seqlens.numel() < 1:
+                raise ValueError("cu_seqlens must be a 1-D tensor of N + 1 offsets, got shape "
+                                 f"{tuple(cu_seqlens.shape)}")
+            if cu_seqlens.dtype not in (torch.int32, torch.int64):
+                raise ValueError(f"cu_seqlens must be int32 or int64, got {cu_seqlens.dtype}")
+            nseq = cu_seqlens.numel() - 1
+        if initial_state is not None and tuple(initial_state.shape) != (nseq, H, dk, dv):
+            raise ValueError(f"Expected initial_state shape {(nseq, H, dk, dv)}, "
                              f"got {tuple(initial_state.shape)}")
-        return self.kernel(q, k, v, g, beta, initial_state)
+        return self.kernel(q, k, v, g, beta, initial_state, cu_seqlens=cu_seqlens)
 
     def eval_roofline(self) -> tuple[int, int]:
         """Dense matmul flops of the chunked WY form and the bytes moved once.
