@@ -197,6 +197,10 @@ int tileops_gdn_prefill_fwd(const void* q, const void* k, const void* v, const f
 int64_t tileops_gdn_varlen_workspace_bytes(int64_t total_len, int64_t num_seqs, int64_t heads,
                                            int64_t dim_k, int64_t dim_v);
 
+/* Flags of tileops_gdn_prefill_varlen_fwd. */
+#define TILEOPS_GDN_QK_L2NORM 1 /* use q / sqrt(|q|^2 + 1e-6), k likewise (fla's
+                                   use_qk_l2norm_in_kernel), fused: no extra pass */
+
 /* Variable-length form of tileops_gdn_prefill_fwd (the fla `cu_seqlens`
  * convention, batch 1): num_seqs sequences packed along one token axis,
  * sequence n being rows [cu_seqlens[n], cu_seqlens[n+1]) of q, k (total_len,
@@ -206,18 +210,22 @@ int64_t tileops_gdn_varlen_workspace_bytes(int64_t total_len, int64_t num_seqs, 
  * it is never copied to the host, so the call does not synchronise.  A
  * cu_seqlens that breaks these rules cannot make the kernels access memory
  * out of range (offsets are clamped) but gives meaningless results, and the
- * device error flag reads 2 (tileops_device_error_flag).  initial_state
- * (NULL = zeros) and final_state (NULL = not written) are (num_seqs, H, dk,
- * dv) fp32; each sequence starts from its own initial state.  `workspace`
- * holds tileops_gdn_varlen_workspace_bytes() bytes, 16-byte aligned.  Same
- * sizes, dtype and chunk rules as tileops_gdn_prefill_fwd; no reference
- * counterpart (the signature follows fla chunk_gated_delta_rule). */
+ * device error flag reads 2 (tileops_device_error_flag).  cu_seqlens = NULL
+ * means num_seqs sequences of total_len / num_seqs rows each (a uniform batch,
+ * the layout of tileops_gdn_prefill_fwd; total_len must divide evenly).
+ * initial_state (NULL = zeros) and final_state (NULL = not written) are
+ * (num_seqs, H, dk, dv) fp32; each sequence starts from its own initial
+ * state.  flags: 0 or TILEOPS_GDN_QK_L2NORM.  `workspace` holds
+ * tileops_gdn_varlen_workspace_bytes() bytes, 16-byte aligned.  Same sizes,
+ * dtype and chunk rules as tileops_gdn_prefill_fwd; no reference counterpart
+ * (the arguments follow fla chunk_gated_delta_rule). */
 int tileops_gdn_prefill_varlen_fwd(const void* q, const void* k, const void* v, const float* g,
                                    const float* beta, const int32_t* cu_seqlens,
                                    int64_t num_seqs, const float* initial_state, void* o,
                                    float* final_state, void* workspace, int64_t total_len,
                                    int64_t heads, int64_t dim_k, int64_t dim_v,
-                                   int64_t chunk_size, double scale, int dtype, void* stream);
+                                   int64_t chunk_size, double scale, int flags, int dtype,
+                                   void* stream);
 
 /* Same as tileops_gdn_prefill_fwd, but allocates nothing and takes no
  * workspace: for callers that cannot allocate device memory when they call

@@ -220,14 +220,26 @@ def gdn_sequential(q, k, v, g, beta, state0, scale: float):
     return o, s
 
 
-def gdn_prefill_bthd(q, k, v, g, beta, scale: Optional[float] = None, initial_state=None):
+def l2norm_rows(x, eps: float = 1e-6):
+    """``x / sqrt(sum(x^2) + eps)`` over the last dim in fp32, cast back to x's
+    dtype: the q / k normalisation fla applies for use_qk_l2norm_in_kernel
+    (its l2norm forward, eps 1e-6)."""
+    xf = _cpu(x).float()
+    return (xf / torch.sqrt((xf * xf).sum(-1, keepdim=True) + eps)).to(x.dtype)
+
+
+def gdn_prefill_bthd(q, k, v, g, beta, scale: Optional[float] = None, initial_state=None,
+                     qk_l2norm: bool = False):
     """The GDN golden on the op's BTHD layout.
 
     q, k ``(B, T, H, Dk)``, v ``(B, T, H, Dv)``, g / beta ``(B, T, H)``,
-    initial_state ``(B, H, Dk, Dv)`` or None (zeros).  Returns
+    initial_state ``(B, H, Dk, Dv)`` or None (zeros); ``qk_l2norm`` first
+    normalises q and k per token and head (``l2norm_rows``).  Returns
     ``(o (B, T, H, Dv) in v's dtype, final_state (B, H, Dk, Dv) fp32)``.
     """
     q, k, v, g, beta = map(_cpu, (q, k, v, g, beta))
+    if qk_l2norm:
+        q, k = l2norm_rows(q), l2norm_rows(k)
     batch, _, heads, dk = q.shape
     dv = v.shape[-1]
     scale = dk**-0.5 if scale is None else scale
@@ -238,7 +250,7 @@ def gdn_prefill_bthd(q, k, v, g, beta, scale: Optional[float] = None, initial_st
 
 
 def gdn_prefill_varlen(q, k, v, g, beta, cu_seqlens, scale: Optional[float] = None,
-                       initial_state=None):
+                       initial_state=None, qk_l2norm: bool = False):
     """The GDN golden on packed variable-length input (fla's ``cu_seqlens``).
 
     q, k ``(1, T, H, Dk)``, v ``(1, T, H, Dv)``, g / beta ``(1, T, H)`` hold N
@@ -260,7 +272,7 @@ def gdn_prefill_varlen(q, k, v, g, beta, cu_seqlens, scale: Optional[float] = No
             finals.append(torch.zeros(1, heads, dk, dv) if h0 is None else h0.float().clone())
             continue
         o_n, s_n = gdn_prefill_bthd(q[:, a:b], k[:, a:b], v[:, a:b], g[:, a:b], beta[:, a:b],
-                                    scale, h0)
+                                    scale, h0, qk_l2norm)
         o[:, a:b] = o_n
         finals.append(s_n)
     final = torch.cat(finals, 0) if finals else torch.zeros(0, heads, dk, dv)

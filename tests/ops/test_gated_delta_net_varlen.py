@@ -154,3 +154,65 @@ def test_rejects_bad_varlen_arguments():
         op1(*args, torch.zeros(1, 1, 128, 128, device="cuda"), cu_seqlens=_cu([64, 64]))
     with pytest.raises(ValueError, match="int32 or int64"):
         op1(*args, cu_seqlens=_cu([64, 64]).float())
+
+
+@pytest.mark.parametrize("dk, dv", [(128, 128), (64, 64)])
+def test_fused_qk_l2norm_uniform(dk, dv):
+    """use_qk_l2norm_in_kernel on raw (unnormalised) q, k == the golden on
+    q / sqrt(|q|^2 + 1e-6), k likewise (fla's l2norm), batch form."""
+    torch.manual_seed(3)
+    b, t, h = 2, 200, 2
+    q = (torch.randn(b, t, h, dk, device="cuda") * 3).bfloat16()
+    k = (torch.randn(b, t, h, dk, device="cuda") * 0.2).bfloat16()
+    _, _, v, g, beta = GdnPrefillWorkload(b, t, h, dk, dv).gen_inputs()
+    h0 = torch.randn(b, h, dk, dv, device="cuda") * 0.1
+    op = GatedDeltaNetPrefillFwdOp(b, t, h, dk, dv)
+    o, s = op(q, k, v, g, beta, h0, use_qk_l2norm_in_kernel=True)
+    o_ref, s_ref = ref.gdn_prefill_bthd(q, k, v, g, beta, None, h0, qk_l2norm=True)
+    torch.testing.assert_close(o.cpu().float(), o_ref.float(), **TOL)
+    torch.testing.assert_close(s.cpu(), s_ref, **TOL)
+
+
+def test_fused_qk_l2norm_varlen():
+    lengths = [90, 0, 64, 33]
+    q, k, v, g, beta, h0 = _packed(lengths, 2, 128, 128)
+    q = (q.float() * 5).bfloat16()
+    k = (k.float() * 0.5).bfloat16()
+    cu = _cu(lengths)
+    o, s = GatedDeltaNetPrefillFwdOp(1, sum(lengths), 2, 128, 128)(
+        q, k, v, g, beta, h0, cu_seqlens=cu, use_qk_l2norm_in_kernel=True)
+    o_ref, s_ref = ref.gdn_prefill_varlen(q, k, v, g, beta, cu, None, h0, qk_l2norm=True)
+    torch.testing.assert_close(o.cpu().float(), o_ref.float(), **TOL)
+    torch.testing.assert_close(s.cpu(), s_ref, **TOL)
+
+
+def test_fla_style_functional_form():
+    from tileops.ops.linear_attention import chunk_gated_delta_rule
+
+    lengths = [70, 58]
+    q, k, v, g, beta, h0 = _packed(lengths, 2, 128, 128)
+    cu = _cu(lengths).long()
+    o, final = chunk_gated_delta_rule(q, k, v, g, beta, initial_state=h0, cu_seqlens=cu)
+    assert final is None
+    o2, final2 = chunk_gated_delta_rule(q, k, v, g, beta, scale=128 ** -0.5, initial_state=h0,
+                                        output_final_state=True, cu_seqlens=cu)
+    o_op, s_op = _run_varlen(q, k, v, g, beta, cu, h0)
+    assert torch.equal(o, o_op) and torch.equal(o2, o_op) and torch.equal(final2, s_op)
+
+
+def test_general_entry_without_offsets_is_the_batched_path():
+    """tileops_gdn_prefill_varlen_fwd with cu_seqlens = NULL runs num_seqs
+    sequences of total / num_seqs rows: bit-equal to tileops_gdn_prefill_fwd."""
+    b, t, h, d = 2, 160, 2, 128
+    q, k, v, g, beta = GdnPrefillWorkload(b, t, h, d, d).gen_inputs()
+    o_ref, s_ref = _run_one(q, k, v, g, beta)
+    lib = nat.lib()
+    ws = torch.empty(lib.tileops_gdn_varlen_workspace_bytes(b * t, b, h, d, d),
+                     dtype=torch.uint8, device="cuda")
+    o = torch.empty_like(v)
+    s = torch.empty(b, h, d, d, device="cuda")
+    nat.launch("tileops_gdn_prefill_varlen_fwd", q.device, nat.ptr(q), nat.ptr(k), nat.ptr(v),
+               nat.ptr(g), nat.ptr(beta), nat.ptr(None), b, nat.ptr(None), nat.ptr(o),
+               nat.ptr(s), nat.ptr(ws), b * t, h, d, d, 64, d ** -0.5, 0,
+               nat.dtype_code(torch.bfloat16))
+    assert torch.equal(o, o_ref) and torch.equal(s, s_ref)

@@ -105,12 +105,17 @@ def test_gdn_varlen_workspace_and_validation():
     head = [NULL] * 5 + [NULL]  # q, k, v, g, beta, cu_seqlens
     tail = [NULL] * 4           # initial_state, o, final_state, workspace
     # no sequences: nothing to do
-    assert fn(*head, 0, *tail, 0, 2, 128, 128, 64, 0.1, 2, NULL) == _native.OK
-    assert fn(*head, 2, *tail, 128, 2, 128, 128, 32, 0.1, 2, NULL) == _native.EBADSHAPE
-    assert fn(*head, 2, *tail, 128, 2, 128, 128, 64, 0.1, 1, NULL) == _native.EBADDTYPE
-    assert fn(*head, 2, *tail, 128, 2, 96, 128, 64, 0.1, 2, NULL) == _native.EBADSHAPE
-    assert fn(*head, -1, *tail, 128, 2, 128, 128, 64, 0.1, 2, NULL) == _native.EBADSHAPE
-    assert fn(*head, 2, *tail, 128, 2, 128, 128, 64, 0.1, 2, NULL) == _native.EINVAL
+    assert fn(*head, 0, *tail, 0, 2, 128, 128, 64, 0.1, 0, 2, NULL) == _native.OK
+    assert fn(*head, 2, *tail, 128, 2, 128, 128, 32, 0.1, 0, 2, NULL) == _native.EBADSHAPE
+    assert fn(*head, 2, *tail, 128, 2, 128, 128, 64, 0.1, 0, 1, NULL) == _native.EBADDTYPE
+    assert fn(*head, 2, *tail, 128, 2, 96, 128, 64, 0.1, 0, 2, NULL) == _native.EBADSHAPE
+    assert fn(*head, -1, *tail, 128, 2, 128, 128, 64, 0.1, 0, 2, NULL) == _native.EBADSHAPE
+    # unknown flag bits
+    assert fn(*head, 2, *tail, 128, 2, 128, 128, 64, 0.1, 4, 2, NULL) == _native.EINVAL
+    # cu_seqlens NULL: total_len must split evenly into num_seqs sequences
+    assert fn(*head, 3, *tail, 128, 2, 128, 128, 64, 0.1, 0, 2, NULL) == _native.EBADSHAPE
+    # NULL tensors
+    assert fn(*head, 2, *tail, 128, 2, 128, 128, 64, 0.1, 1, 2, NULL) == _native.EINVAL
 
 
 def test_gdn_workspace_and_validation():

@@ -238,14 +238,16 @@ struct PrepSmem {
   static constexpr int kKe = kBeta + kC * 4;
   static constexpr int kEgp = kKe + kC * 4;     // e^gc
   static constexpr int kEgm = kEgp + kC * 4;    // e^-gc, and the factor flag after it
+  static constexpr int kRk = kEgm + kC * 4 + 16;  // 1 / |k_l| (fused q/k L2 norm)
+  static constexpr int kRq = kRk + kC * 4;        // 1 / |q_l|
   // two mbarriers, the abort flag, then the chunk's (map row, map batch,
   // head, first row to zero) read back late instead of held in registers
-  static constexpr int kBar = kEgm + kC * 4 + 16;
+  static constexpr int kBar = kRq + kC * 4;
   static constexpr int kBytes = kBar + 48;
   static constexpr int kAlloc = kBytes + 1024;  // room to align the base to 1 KB
 };
 
-template <int DK, int DV, bool kVar>
+template <int DK, int DV, bool kVar, bool kNorm>
 __global__ void __launch_bounds__(128, 4)
     gdn_prepare(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                 const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_wk,
@@ -266,6 +268,8 @@ __global__ void __launch_bounds__(128, 4)
   float* egp = reinterpret_cast<float*>(sm + L::kEgp);
   float* egm = reinterpret_cast<float*>(sm + L::kEgm);
   int* fact_flag = reinterpret_cast<int*>(sm + L::kEgm + kC * 4);
+  float* rk = reinterpret_cast<float*>(sm + L::kRk);
+  float* rq = reinterpret_cast<float*>(sm + L::kRq);
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + L::kBar);       // K, Q
   uint64_t* bar_v = reinterpret_cast<uint64_t*>(sm + L::kBar + 8);  // V
   volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + L::kBar + 16);
@@ -361,6 +365,28 @@ __global__ void __launch_bounds__(128, 4)
     zero_rows(sm + L::kQs, DK / 64, zpad);
     __syncthreads();
   }
+  if constexpr (kNorm) {
+    // Fused q / k L2 norm: 1 / sqrt(sum x^2 + 1e-6) per row (thread t: row
+    // t % 64 of K for t < 64, of Q otherwise).  Nothing is rewritten; the
+    // factors scale the products and the per-row workspace tail below.
+    const int row = tid & 63;
+    const uint8_t* tile = sm + (tid < 64 ? L::kKs : L::kQs) + row * 128;
+    float ss = 0.0f;
+#pragma unroll
+    for (int bx = 0; bx < DK / 64; ++bx)
+#pragma unroll
+      for (int u8 = 0; u8 < 8; ++u8) {
+        const uint4 pk = *reinterpret_cast<const uint4*>(tile + bx * 8192 + u8 * 16);
+        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&pk);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(h2[e]);
+          ss = fmaf(f.x, f.x, fmaf(f.y, f.y, ss));
+        }
+      }
+    (tid < 64 ? rk : rq)[row] = 1.0f / sqrtf(ss + 1e-6f);
+    __syncthreads();
+  }
 
   // ---- KK^T -> A (strictly lower, fp32) and QK^T -> QKm (lower, bf16, to the
   // workspace); warp w owns rows 16w..16w+15 and only needs columns <= them.
@@ -405,6 +431,13 @@ __global__ void __launch_bounds__(128, 4)
           d0 = s <= l ? __expf(gl - gc[s]) : 0.0f;
           d1 = s + 1 <= l ? __expf(gl - gc[s + 1]) : 0.0f;
         }
+        if constexpr (kNorm) {  // k_l . k_s / (|k_l| |k_s|), q_l . k_s / (|q_l| |k_s|)
+          const float rkl = rk[l], rql = rq[l], rk0 = rk[s], rk1 = rk[s + 1];
+          ak[n][half * 2] *= rkl * rk0;
+          ak[n][half * 2 + 1] *= rkl * rk1;
+          aq[n][half * 2] *= rql * rk0;
+          aq[n][half * 2 + 1] *= rql * rk1;
+        }
         As[l * kLdA + s] = s < l ? bl * d0 * ak[n][half * 2] : 0.0f;
         As[l * kLdA + s + 1] = s + 1 < l ? bl * d1 * ak[n][half * 2 + 1] : 0.0f;
         *reinterpret_cast<uint32_t*>(wsc + W::kQK + l * kC + s) =
@@ -433,9 +466,13 @@ __global__ void __launch_bounds__(128, 4)
     const int i = tid - 64;
     const float gl = gc[kC - 1];
     const float e = __expf(gc[i]);
-    ke[i] = bt[i] * e;
-    wsf[W::kQsc + i] = scale * e;
-    wsf[W::kDec + i] = __expf(gl - gc[i]);
+    // With the fused norm, 1/|k_i| joins the factors that multiply row i of K
+    // (Wk = T diag(ke) K here, K^T (dec err) in the scan) and 1/|q_i| the one
+    // that multiplies row i of Q S.
+    const float nk = kNorm ? rk[i] : 1.0f, nq = kNorm ? rq[i] : 1.0f;
+    ke[i] = bt[i] * e * nk;
+    wsf[W::kQsc + i] = scale * e * nq;
+    wsf[W::kDec + i] = __expf(gl - gc[i]) * nk;
     if (i < 4) wsf[W::kEgl + i] = i == 0 ? __expf(gl) : 0.0f;
   }
   __syncthreads();
@@ -1235,11 +1272,11 @@ __global__ void __launch_bounds__(kScanTcThreads, 1)
 // map_rows, map_batch): (T, B) for a uniform batch, (total, 1) for packed
 // sequences.  For variable length, sl.chunk_seq points at nslots ints the
 // index kernel fills first.
-template <int DK, int DV, bool kVar>
+template <int DK, int DV, bool kVar, bool kNorm>
 int launch_gdn(const void* q, const void* k, const void* v, const float* g, const float* beta,
                const float* h0, void* o, float* hT, void* ws, SeqLayout sl, int nseq,
                int map_rows, int map_batch, int H, float scale, cudaStream_t s) {
-  auto k1 = gdn_prepare<DK, DV, kVar>;
+  auto k1 = gdn_prepare<DK, DV, kVar, kNorm>;
   auto k2 = gdn_scan<DK, DV, kVar>;
   CUtensorMap tq, tk, tv;
   if (!make_bshd_map(&tq, q, DK, H, map_rows, map_batch, kC, true) ||
@@ -1315,21 +1352,21 @@ int64_t varlen_table_offset(int64_t total_len, int64_t num_seqs, int64_t heads, 
   return heads * varlen_slots(total_len, num_seqs) * per;
 }
 
-template <bool kVar>
+template <bool kVar, bool kNorm>
 int dispatch_gdn(const void* q, const void* k, const void* v, const float* g, const float* beta,
                  const float* h0, void* o, float* hT, void* ws, SeqLayout sl, int nseq,
                  int map_rows, int map_batch, int H, int dim_k, int dim_v, float scale,
                  cudaStream_t s) {
   if (dim_k == 128 && dim_v == 128)
-    return launch_gdn<128, 128, kVar>(q, k, v, g, beta, h0, o, hT, ws, sl, nseq, map_rows, map_batch,
+    return launch_gdn<128, 128, kVar, kNorm>(q, k, v, g, beta, h0, o, hT, ws, sl, nseq, map_rows, map_batch,
                                 H, scale, s);
   if (dim_k == 64 && dim_v == 64)
-    return launch_gdn<64, 64, kVar>(q, k, v, g, beta, h0, o, hT, ws, sl, nseq, map_rows, map_batch, H,
+    return launch_gdn<64, 64, kVar, kNorm>(q, k, v, g, beta, h0, o, hT, ws, sl, nseq, map_rows, map_batch, H,
                               scale, s);
   if (dim_k == 128 && dim_v == 64)
-    return launch_gdn<128, 64, kVar>(q, k, v, g, beta, h0, o, hT, ws, sl, nseq, map_rows, map_batch,
+    return launch_gdn<128, 64, kVar, kNorm>(q, k, v, g, beta, h0, o, hT, ws, sl, nseq, map_rows, map_batch,
                                H, scale, s);
-  return launch_gdn<64, 128, kVar>(q, k, v, g, beta, h0, o, hT, ws, sl, nseq, map_rows, map_batch, H,
+  return launch_gdn<64, 128, kVar, kNorm>(q, k, v, g, beta, h0, o, hT, ws, sl, nseq, map_rows, map_batch, H,
                              scale, s);
 }
 
@@ -1367,8 +1404,8 @@ extern "C" int tileops_gdn_prefill_fwd(const void* q, const void* k, const void*
   const int B = static_cast<int>(batch), T = static_cast<int>(seq_len);
   const int nchunks = (T + kC - 1) / kC;
   const SeqLayout sl{nullptr, nullptr, T, nchunks, B * nchunks};
-  return dispatch_gdn<false>(q, k, v, g, beta, initial_state, o, final_state, workspace, sl, B, T,
-                             B,
+  return dispatch_gdn<false, false>(q, k, v, g, beta, initial_state, o, final_state, workspace,
+                                    sl, B, T, B,
                       static_cast<int>(heads), static_cast<int>(dim_k), static_cast<int>(dim_v),
                       static_cast<float>(scale), as_stream(stream));
 }
@@ -1390,7 +1427,7 @@ extern "C" int tileops_gdn_prefill_varlen_fwd(const void* q, const void* k, cons
                                               float* final_state, void* workspace,
                                               int64_t total_len, int64_t heads, int64_t dim_k,
                                               int64_t dim_v, int64_t chunk_size, double scale,
-                                              int dtype, void* stream) {
+                                              int flags, int dtype, void* stream) {
   if (total_len < 0 || num_seqs < 0 || heads <= 0 || total_len > (1 << 30) ||
       num_seqs > (1 << 24) || heads * varlen_slots(total_len, num_seqs) > 0x7fffffffLL ||
       num_seqs * heads > (1 << 24))
@@ -1399,6 +1436,9 @@ extern "C" int tileops_gdn_prefill_varlen_fwd(const void* q, const void* k, cons
   const int64_t per = ws_bytes_per_chunk(dim_k, dim_v);
   if (per < 0) return TILEOPS_EBADSHAPE;
   if (dtype != TILEOPS_DT_BF16) return TILEOPS_EBADDTYPE;
+  if ((flags & ~TILEOPS_GDN_QK_L2NORM) != 0) return TILEOPS_EINVAL;
+  if (cu_seqlens == nullptr && num_seqs > 0 && total_len % num_seqs != 0)
+    return TILEOPS_EBADSHAPE;
   if (num_seqs == 0) return TILEOPS_OK;
   cudaStream_t s = as_stream(stream);
   const int64_t state_bytes = num_seqs * heads * dim_k * dim_v * 4;
@@ -1410,18 +1450,32 @@ extern "C" int tileops_gdn_prefill_varlen_fwd(const void* q, const void* k, cons
                       : cudaMemsetAsync(final_state, 0, state_bytes, s);
     return e == cudaSuccess ? TILEOPS_OK : TILEOPS_ELAUNCH;
   }
-  if (!q || !k || !v || !g || !beta || !o || !workspace || !cu_seqlens) return TILEOPS_EINVAL;
+  if (!q || !k || !v || !g || !beta || !o || !workspace) return TILEOPS_EINVAL;
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || !aligned16(workspace))
     return TILEOPS_EALIGN;
+  const bool norm = (flags & TILEOPS_GDN_QK_L2NORM) != 0;
+  const int H = static_cast<int>(heads), N = static_cast<int>(num_seqs);
+  const int dk = static_cast<int>(dim_k), dv = static_cast<int>(dim_v);
+  const float sc = static_cast<float>(scale);
+  if (cu_seqlens == nullptr) {  // num_seqs sequences of total_len / num_seqs rows each
+    const int T = static_cast<int>(total_len / num_seqs);
+    const int nchunks = (T + kC - 1) / kC;
+    const SeqLayout sl{nullptr, nullptr, T, nchunks, N * nchunks};
+    return norm ? dispatch_gdn<false, true>(q, k, v, g, beta, initial_state, o, final_state,
+                                            workspace, sl, N, T, N, H, dk, dv, sc, s)
+                : dispatch_gdn<false, false>(q, k, v, g, beta, initial_state, o, final_state,
+                                             workspace, sl, N, T, N, H, dk, dv, sc, s);
+  }
   const int64_t nslots = varlen_slots(total_len, num_seqs);
   auto* table = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) +
                                        varlen_table_offset(total_len, num_seqs, heads, per));
   const SeqLayout sl{cu_seqlens, table, static_cast<int>(total_len), 0,
                      static_cast<int>(nslots)};
-  return dispatch_gdn<true>(q, k, v, g, beta, initial_state, o, final_state, workspace, sl,
-                      static_cast<int>(num_seqs), static_cast<int>(total_len), 1,
-                      static_cast<int>(heads), static_cast<int>(dim_k), static_cast<int>(dim_v),
-                      static_cast<float>(scale), s);
+  const int rows = static_cast<int>(total_len);
+  return norm ? dispatch_gdn<true, true>(q, k, v, g, beta, initial_state, o, final_state,
+                                         workspace, sl, N, rows, 1, H, dk, dv, sc, s)
+              : dispatch_gdn<true, false>(q, k, v, g, beta, initial_state, o, final_state,
+                                          workspace, sl, N, rows, 1, H, dk, dv, sc, s);
 }
 
 // ------------------------------------------------------------------------

@@ -71,7 +71,7 @@ class GDNPrefillFwdKernel(Kernel):
         return int(n)
 
     def forward(self, q, k, v, g, beta, initial_state=None, output_final_state: bool = True,
-                cu_seqlens=None):
+                cu_seqlens=None, use_qk_l2norm_in_kernel: bool = False):
         q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
         g = g.contiguous().float()
         beta = beta.contiguous().float()
@@ -84,7 +84,7 @@ class GDNPrefillFwdKernel(Kernel):
         final = (torch.empty((nseq, self.heads, self.dim_k, self.dim_v),
                              dtype=torch.float32, device=q.device)
                  if output_final_state else None)
-        if cu_seqlens is None:
+        if cu_seqlens is None and not use_qk_l2norm_in_kernel:
             ws = torch.empty(max(self.workspace_bytes(), 16), dtype=torch.uint8,
                              device=q.device)
             _native.launch(
@@ -96,15 +96,19 @@ class GDNPrefillFwdKernel(Kernel):
                 float(self.scale), _native.dtype_code(self.dtype),
             )
             return o, final
-        cu = cu_seqlens.to(device=q.device, dtype=torch.int32).contiguous()
+        # The general entry: packed sequences (cu_seqlens) and / or the fused
+        # q / k L2 norm; without cu_seqlens it runs `batch` sequences of seq_len.
+        cu = (None if cu_seqlens is None
+              else cu_seqlens.to(device=q.device, dtype=torch.int32).contiguous())
         ws = torch.empty(max(self.varlen_workspace_bytes(nseq), 16), dtype=torch.uint8,
                          device=q.device)
+        flags = _native.GDN_QK_L2NORM if use_qk_l2norm_in_kernel else 0
         _native.launch(
             "tileops_gdn_prefill_varlen_fwd", q.device,
             _native.ptr(q), _native.ptr(k), _native.ptr(v), _native.ptr(g), _native.ptr(beta),
             _native.ptr(cu), nseq, _native.ptr(initial_state), _native.ptr(o),
             _native.ptr(final), _native.ptr(ws),
             self.batch * self.seq_len, self.heads, self.dim_k, self.dim_v, self.chunk_size,
-            float(self.scale), _native.dtype_code(self.dtype),
+            float(self.scale), flags, _native.dtype_code(self.dtype),
         )
         return o, final

@@ -1,3 +1,6 @@
-from tileops.ops.linear_attention.gated_delta_net_prefill import GatedDeltaNetPrefillFwdOp
+from tileops.ops.linear_attention.gated_delta_net_prefill import (
+    GatedDeltaNetPrefillFwdOp,
+    chunk_gated_delta_rule,
+)
 
-__all__ = ["GatedDeltaNetPrefillFwdOp"]
+__all__ = ["GatedDeltaNetPrefillFwdOp", "chunk_gated_delta_rule"]

@@ -9,7 +9,8 @@ API in the style of the other ops:
 
     GatedDeltaNetPrefillFwdOp(batch, seq_len, heads, dim_k, dim_v, chunk_size=64,
                               scale=None, dtype=torch.bfloat16, kernel_map=None)
-    forward(q, k, v, g, beta, initial_state=None, cu_seqlens=None) -> (o, final_state)
+    forward(q, k, v, g, beta, initial_state=None, cu_seqlens=None,
+            use_qk_l2norm_in_kernel=False) -> (o, final_state)
 
 Layout BTHD (the fla convention): q, k (B, T, H, dk), v (B, T, H, dv) bf16; g
 (B, T, H) fp32 per-token log decay (<= 0 for decay); beta (B, T, H) fp32;
@@ -20,7 +21,11 @@ initial_state continues the sequence (chunked prefill of long contexts).
 Variable-length input follows fla's ``cu_seqlens`` convention: batch 1, the N
 sequences packed along the token axis, ``cu_seqlens`` an integer device tensor
 of N + 1 offsets (0, ..., T); initial_state and the final state are then
-(N, H, dk, dv), one per sequence.
+(N, H, dk, dv), one per sequence.  ``use_qk_l2norm_in_kernel`` uses
+q / sqrt(|q|^2 + 1e-6) and k likewise per token and head (fla's l2norm), fused
+into the kernels: q and k are read once, never rewritten.
+
+``chunk_gated_delta_rule`` is the fla-style functional form.
 """
 
 from __future__ import annotations
@@ -34,7 +39,7 @@ from tileops.kernels.kernel_base import Kernel
 from tileops.kernels.linear_attention import GDNPrefillFwdKernel
 from tileops.ops.op_base import Op
 
-__all__ = ["GatedDeltaNetPrefillFwdOp"]
+__all__ = ["GatedDeltaNetPrefillFwdOp", "chunk_gated_delta_rule"]
 
 
 class GatedDeltaNetPrefillFwdOp(Op):
@@ -67,7 +72,8 @@ class GatedDeltaNetPrefillFwdOp(Op):
 
     def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor,
                 beta: torch.Tensor, initial_state: Optional[torch.Tensor] = None,
-                cu_seqlens: Optional[torch.Tensor] = None):
+                cu_seqlens: Optional[torch.Tensor] = None,
+                use_qk_l2norm_in_kernel: bool = False):
         backend = get_device_backend()
         for name, t in (("q", q), ("k", k), ("v", v), ("g", g), ("beta", beta),
                         ("initial_state", initial_state), ("cu_seqlens", cu_seqlens)):
@@ -97,7 +103,8 @@ class GatedDeltaNetPrefillFwdOp(Op):
         if initial_state is not None and tuple(initial_state.shape) != (nseq, H, dk, dv):
             raise ValueError(f"Expected initial_state shape {(nseq, H, dk, dv)}, "
                              f"got {tuple(initial_state.shape)}")
-        return self.kernel(q, k, v, g, beta, initial_state, cu_seqlens=cu_seqlens)
+        return self.kernel(q, k, v, g, beta, initial_state, cu_seqlens=cu_seqlens,
+                           use_qk_l2norm_in_kernel=use_qk_l2norm_in_kernel)
 
     def eval_roofline(self) -> tuple[int, int]:
         """Dense matmul flops of the chunked WY form and the bytes moved once.
@@ -115,3 +122,25 @@ class GatedDeltaNetPrefillFwdOp(Op):
         nbytes = (tokens * (2 * dk + 2 * dv) * eb + tokens * 2 * 4
                   + self.batch * self.heads * dk * dv * 4)
         return int(flops), int(nbytes)
+
+
+def chunk_gated_delta_rule(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor,
+                           beta: torch.Tensor, scale: Optional[float] = None,
+                           initial_state: Optional[torch.Tensor] = None,
+                           output_final_state: bool = False,
+                           use_qk_l2norm_in_kernel: bool = False,
+                           cu_seqlens: Optional[torch.Tensor] = None):
+    """fla-style functional form (``fla.ops.gated_delta_rule.chunk_gated_delta_rule``
+    argument names and order, BTHD layout, chunk 64).
+
+    Returns ``(o, final_state)``; final_state is None unless output_final_state.
+    """
+    if q.dim() != 4 or v.dim() != 4:
+        raise ValueError(f"Expected q (B, T, H, K) and v (B, T, H, V), got {tuple(q.shape)} "
+                         f"and {tuple(v.shape)}")
+    batch, seq_len, heads, dim_k = q.shape
+    op = GatedDeltaNetPrefillFwdOp(batch, seq_len, heads, dim_k, v.shape[-1], scale=scale,
+                                   dtype=q.dtype)
+    o, final = op(q, k, v, g, beta, initial_state, cu_seqlens=cu_seqlens,
+                  use_qk_l2norm_in_kernel=use_qk_l2norm_in_kernel)
+    return o, (final if output_final_state else None)
