@@ -300,6 +300,41 @@ def _gdn() -> Workload:
     )
 
 
+def _gla() -> Workload:
+    from tileops.ops.linear_attention import GLADecodeOp
+
+    B, H, DK, DV = 8, 32, 128, 128
+
+    def make(dev, seed):
+        g = torch.Generator(device="cpu").manual_seed(seed)
+        q = torch.randn(B, H, DK, generator=g) * 0.5
+        k = torch.randn(B, H, DK, generator=g) * 0.5
+        v = torch.randn(B, H, DV, generator=g) * 0.5
+        gk = -torch.rand(B, H, DK, generator=g)
+        state = torch.randn(B, H, DK, DV, generator=g)
+        return tuple(t.to(torch.bfloat16).to(dev) for t in (q, k, v, gk, state))
+
+    def cpu(inp):
+        from oracle import reference as ref
+
+        return ref.gla_decode(*inp, DK ** -0.5)
+
+    def units(inp):
+        b, h = inp[0].shape[:2]
+        return float(b * h * (3 * DK + 2 * DV + 2 * DK * DV) * 2)
+
+    return Workload(
+        name="gla_decode", metric="achieved HBM GB/s (GLADecodeOp)", unit="GB/s",
+        dtype="bf16",
+        config={"workload": "GLADecodeOp B=8 H=32 DK=DV=128 bf16, one decode step (the "
+                            "reference test's largest serving case, serving-b8-h32)"},
+        make_inputs=make, build_op=lambda: GLADecodeOp(B, H, DK, DV, dtype=torch.bfloat16),
+        run=lambda op, inp: op(*inp), work_per_step=lambda op: float(op.eval_roofline()[1]),
+        kernel_regex="gla_decode", cpu_fn=cpu,
+        cpu_slice=lambda inp, rows: tuple(t[:1] for t in inp), cpu_units=units,
+    )
+
+
 def workloads() -> dict[str, Callable[[], Workload]]:
     table = {
         "fused_add_layer_norm": _faln,
@@ -310,6 +345,7 @@ def workloads() -> dict[str, Callable[[], Workload]]:
         "mha": lambda: _mha(False),
         "mha_causal": lambda: _mha(True),
         "gdn": _gdn,
+        "gla_decode": _gla,
     }
     for kind in ("hardswish", "hardsigmoid", "clamp_scalar", "isnan", "isinf", "isfinite",
                  "bitwise_not"):
@@ -494,7 +530,7 @@ def run_ours(args, wl: Workload) -> Optional[dict]:
     outs = out if isinstance(out, (tuple, list)) else (out,)
     set_bytes += sum(t.numel() * t.element_size() for t in outs)
     del out, outs
-    n_sets = max(2, min(8, -(-3 * L2_BYTES // max(set_bytes, 1)) + 1))
+    n_sets = max(2, min(32, -(-3 * L2_BYTES // max(set_bytes, 1)) + 1))
     sets = [probe] + [wl.make_inputs(device, 1235 + rank + 1000 * i) for i in range(1, n_sets)]
     work = wl.work_per_step(op)
     stream = torch.cuda.current_stream(device)

@@ -165,6 +165,20 @@ int tileops_mha_fwd(const void* q, const void* k, const void* v, void* o, float*
                     int64_t seq_kv, int64_t dim, int is_causal, double sm_scale, int dtype,
                     void* stream);
 
+/* ---- gated linear attention decode ------------------------------------- */
+
+/* One recurrent step per (b, h): new_state[i, j] = exp(gk[i]) state[i, j] +
+ * k[i] v[j];  o[j] = scale * sum_i q[i] new_state[i, j], fp32 math, o from the
+ * fp32 new state, both outputs rounded to `dtype` (f32/f16/bf16).  Layout BHD:
+ * q, k, gk (B, H, DK); v, o (B, H, DV); state, new_state (B, H, DK, DV).
+ * scale <= 0 means DK^-0.5.  new_state may not alias state.
+ * Replaces _gla_decode_kernel,
+ * kernels/linear_attention/gla_decode/gla_decode_kernel/_gla_decode_kernel.py:57. */
+int tileops_gla_decode_fwd(const void* q, const void* k, const void* v, const void* gk,
+                           const void* state, void* o, void* new_state, int64_t batch,
+                           int64_t heads, int64_t dim_k, int64_t dim_v, double scale, int dtype,
+                           void* stream);
+
 /* ---- gated delta net (linear attention) -------------------------------- */
 
 /* Bytes of scratch workspace tileops_gdn_prefill_fwd needs for this shape

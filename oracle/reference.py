@@ -277,3 +277,19 @@ def gdn_prefill_varlen(q, k, v, g, beta, cu_seqlens, scale: Optional[float] = No
         finals.append(s_n)
     final = torch.cat(finals, 0) if finals else torch.zeros(0, heads, dk, dv)
     return o, final
+
+
+# ------------------------------------------------------ GLA decode
+def gla_decode(q, k, v, gk, state, scale: float):
+    """One gated-linear-attention decode step in fp32.
+
+    Restates golden_gla_decode,
+    examples/TileOPs/tileops/kernels/linear_attention/gla_decode/gla_decode_kernel/
+    _gla_decode_kernel.py:211-218 (layout BHD): new_state = exp(gk)[..., None]
+    * state + k (x) v; o = scale * q^T new_state.  Returns ``(o, new_state)``
+    in fp32.
+    """
+    qf, kf, vf, gf, sf = (_cpu(t).float() for t in (q, k, v, gk, state))
+    new_state = sf * torch.exp(gf)[..., None] + kf[..., :, None] * vf[..., None, :]
+    o = scale * torch.einsum("bhk,bhkv->bhv", qf, new_state)
+    return o, new_state

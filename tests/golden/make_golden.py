@@ -37,6 +37,7 @@ import torch.nn.functional as F
 
 HERE = Path(__file__).resolve().parent
 SEED = 1235
+ONLY: list[str] = []  # name prefixes to write (empty: all)
 
 
 class RefSource:
@@ -82,6 +83,8 @@ class RefSource:
 
 
 def save(name: str, inputs: dict, outputs: dict, meta: dict) -> None:
+    if ONLY and not any(name.startswith(p) for p in ONLY):
+        return
     path = HERE / f"{name}.pt"
     torch.save({"inputs": inputs, "outputs": outputs, "meta": meta}, path)
     size = path.stat().st_size
@@ -100,7 +103,10 @@ def corner_values(dtype: torch.dtype) -> torch.Tensor:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference", type=Path)
+    ap.add_argument("--only", nargs="*", default=[],
+                    help="write only fixtures whose name starts with one of these")
     args = ap.parse_args()
+    ONLY.extend(args.only)
     src = RefSource(args.reference)
     sys.path.insert(0, str(src.to))
     from tileops.workloads.attention import MhaFwdWorkload
@@ -298,6 +304,34 @@ def main() -> None:
              "beta": beta, "state0": s0}, {"o": o, "final_state": s},
              {"source": "gdn_prefill_probe.py:golden_gdn_sequential", "layout": "BHTD",
               "scale": scale, "seed": 0, "qk_l2norm": l2})
+
+    # ---- GLA decode: the reference workload's inputs and its golden ----
+    # GLADecodeWorkload (tileops/workloads/linear_attention.py:19-64) imports
+    # torch_npu through the kernel module, so its gen_inputs and the golden
+    # are compiled out of the source like the reference programs above.
+    gen = src.method("examples/TileOPs/tileops/workloads/linear_attention.py",
+                     "GLADecodeWorkload", "gen_inputs")
+    gen.__globals__["get_device_backend"] = lambda: types.SimpleNamespace(name="cpu")
+    gold = src.function(K + "linear_attention/gla_decode/gla_decode_kernel/_gla_decode_kernel.py",
+                        "golden_gla_decode")
+    # The reference test's cases (tests/ops/test_gla_decode.py:26-36) except
+    # the two largest serving shapes (kept out of the fixture size budget).
+    for b_, h_, dk, dv, dt, sc in [(2, 4, 64, 64, torch.float16, -1.0),
+                                   (2, 4, 64, 64, torch.bfloat16, -1.0),
+                                   (1, 8, 128, 128, torch.bfloat16, -1.0),
+                                   (1, 2, 32, 16, torch.float32, -1.0),
+                                   (2, 3, 16, 16, torch.float16, -1.0),
+                                   (1, 4, 128, 64, torch.float16, -1.0),
+                                   (2, 3, 64, 64, torch.bfloat16, 0.25)]:
+        torch.manual_seed(SEED)
+        scale = sc if sc > 0 else dk**-0.5
+        wl = types.SimpleNamespace(B=b_, H=h_, DK=dk, DV=dv, dtype=dt)
+        q, k, v, gk, state = gen(wl)
+        o, ns = gold(q, k, v, gk, state, scale)
+        save(f"gla_decode_b{b_}_h{h_}_k{dk}_v{dv}_{dn[dt]}" + ("_s025" if sc > 0 else ""),
+             {"q": q, "k": k, "v": v, "gk": gk, "state": state}, {"o": o, "new_state": ns},
+             {"source": "_gla_decode_kernel.py:golden_gla_decode", "scale": scale,
+              "scale_arg": sc, "seed": SEED})
 
 
 if __name__ == "__main__":

@@ -142,3 +142,12 @@ def test_oracle_gdn_varlen_matches_batched_golden():
     torch.testing.assert_close(o, torch.cat([o_b[0:1], o_b[1:2]], 1), atol=0, rtol=0)
     torch.testing.assert_close(s[[0, 2]], s_b, atol=0, rtol=0)
     torch.testing.assert_close(s[1], h0[1], atol=0, rtol=0)
+
+
+@pytest.mark.parametrize("name", names("gla_decode_"))
+def test_oracle_gla_decode(name):
+    case = load(name)
+    i, m = case["inputs"], case["meta"]
+    o, ns = ref.gla_decode(i["q"], i["k"], i["v"], i["gk"], i["state"], m["scale"])
+    assert_same(o, case["outputs"]["o"])
+    assert_same(ns, case["outputs"]["new_state"])
