@@ -335,6 +335,50 @@ def _gla() -> Workload:
     )
 
 
+def _ssd() -> Workload:
+    from tileops.ops.mamba import SSDChunkScanFwdOp
+
+    B, NC, Q, H, P, N, G = 4, 8, 256, 80, 64, 128, 1
+    S = NC * Q
+
+    def make(dev, seed):
+        g = torch.Generator(device="cpu").manual_seed(seed)
+        x = (torch.randn(B, S, H, P, generator=g) * 0.1).to(torch.bfloat16)
+        cb = (torch.randn(B, NC, G, Q, Q, generator=g) * 0.1).to(torch.bfloat16)
+        dA = -torch.rand(B, H, NC, Q, generator=g).cumsum(-1)
+        Cm = (torch.randn(B, S, G, N, generator=g) * 0.1).to(torch.bfloat16)
+        prev = torch.randn(B, NC, H, P, N, generator=g) * 0.1
+        dt = (torch.rand(B, H, NC, Q, generator=g) * 0.1 + 0.01).to(torch.bfloat16)
+        return tuple(t.to(dev) for t in (x, cb, dA, Cm, prev, dt))
+
+    def cpu(inp):
+        from oracle import reference as ref
+
+        return ref.ssd_chunk_scan(*inp, G)
+
+    def sample(inp, rows):  # one chunk of batch 0, all heads
+        x, cb, dA, Cm, prev, dt = inp
+        return (x[:1, :Q], cb[:1, :1], dA[:1, :, :1], Cm[:1, :Q], prev[:1, :1], dt[:1, :, :1])
+
+    def units(inp):  # bytes of the sample by the op's formula
+        x, cb, dA, Cm, prev, dt = inp
+        b, s, h, pp = x.shape
+        tok = b * s * h
+        return float(tok * pp * 2 + cb.numel() * 2 + tok * 4 + Cm.numel() * 2 + prev.numel() * 4
+                     + tok * 2 + tok * pp * 4)
+
+    return Workload(
+        name="ssd_chunk_scan", metric="achieved HBM GB/s (SSDChunkScanFwdOp)", unit="GB/s",
+        dtype="bf16",
+        config={"workload": "SSDChunkScanFwdOp x (4, 2048, 80, 64) bf16, chunk 256, d_state "
+                            "128, 1 group (manifest mamba2-2p7b-b4-s2k)"},
+        make_inputs=make, build_op=SSDChunkScanFwdOp,
+        run=lambda op, inp: op(*inp),
+        work_per_step=lambda op: float(op.eval_roofline()[1]),
+        kernel_regex="ssd_chunk_scan", cpu_fn=cpu, cpu_slice=sample, cpu_units=units,
+    )
+
+
 def workloads() -> dict[str, Callable[[], Workload]]:
     table = {
         "fused_add_layer_norm": _faln,
@@ -346,6 +390,7 @@ def workloads() -> dict[str, Callable[[], Workload]]:
         "mha_causal": lambda: _mha(True),
         "gdn": _gdn,
         "gla_decode": _gla,
+        "ssd_chunk_scan": _ssd,
     }
     for kind in ("hardswish", "hardsigmoid", "clamp_scalar", "isnan", "isinf", "isfinite",
                  "bitwise_not"):

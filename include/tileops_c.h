@@ -179,6 +179,24 @@ int tileops_gla_decode_fwd(const void* q, const void* k, const void* v, const vo
                            int64_t heads, int64_t dim_k, int64_t dim_v, double scale, int dtype,
                            void* stream);
 
+/* ---- Mamba-2 SSD chunk scan --------------------------------------------- */
+
+/* out[l, p] = exp(dA[l]) * sum_n C[l, n] prev[p, n]
+ *           + sum_{s <= l} cb[l, s] exp(dA[l] - dA[s]) dt[s] x[s, p]
+ * per batch, chunk and head (group g = h / (H / G)), fp32 accumulation on
+ * tcgen05 tensor cores.  x (B, NC*Q, H, P), C (B, NC*Q, G, N), cb (B, NC, G,
+ * Q, Q) and dt (B, H, NC, Q) in `dtype` (f16/bf16); dA_cumsum (B, H, NC, Q)
+ * and prev_states (B, NC, H, P, N) fp32; out (B, NC*Q, H, P) fp32.  P a
+ * multiple of 16 up to 128, N a multiple of 8 up to 256, Q up to 1024; x, C,
+ * cb, prev_states, out 16-byte aligned.  prev_states enter the MMA rounded to
+ * `dtype`.  Replaces _ssd_chunk_scan_fwd_kernel,
+ * kernels/mamba/ssd_chunk_scan/ssd_chunk_scan_kernel/perf_opt/_ssd_chunk_scan_fwd_kernel.py:181. */
+int tileops_ssd_chunk_scan_fwd(const void* x, const void* cb, const float* dA_cumsum,
+                               const void* C, const float* prev_states, const void* dt,
+                               float* out, int64_t batch, int64_t num_chunks, int64_t chunk_len,
+                               int64_t n_heads, int64_t d_head, int64_t d_state,
+                               int64_t n_groups, int dtype, void* stream);
+
 /* ---- gated delta net (linear attention) -------------------------------- */
 
 /* Bytes of scratch workspace tileops_gdn_prefill_fwd needs for this shape

@@ -293,3 +293,33 @@ def gla_decode(q, k, v, gk, state, scale: float):
     new_state = sf * torch.exp(gf)[..., None] + kf[..., :, None] * vf[..., None, :]
     o = scale * torch.einsum("bhk,bhkv->bhv", qf, new_state)
     return o, new_state
+
+
+# ------------------------------------------------------ Mamba-2 SSD chunk scan
+def ssd_chunk_scan(x, cb, dA_cumsum, C, prev_states, dt, n_groups: int):
+    """Fused SSD chunk output in fp32.
+
+    Restates golden_ssd_chunk_scan_fwd,
+    examples/TileOPs/tileops/kernels/mamba/ssd_chunk_scan/ssd_chunk_scan_kernel/perf_opt/
+    _ssd_chunk_scan_fwd_kernel.py:123-178:
+    out[l, p] = exp(dA[l]) sum_n C[l, n] prev[p, n]
+              + sum_{s <= l} cb[l, s] exp(dA[l] - dA[s]) dt[s] x[s, p],
+    per batch, chunk and head (group h // (H // G)).  Layouts: x (B, S, H, P),
+    cb (B, NC, G, L, L), dA_cumsum (B, H, NC, L), C (B, S, G, N), prev_states
+    (B, NC, H, P, N), dt (B, H, NC, L); returns (B, S, H, P) fp32.
+    """
+    x, cb, dA_cumsum, C, prev_states, dt = map(_cpu, (x, cb, dA_cumsum, C, prev_states, dt))
+    b, seq, h, p = x.shape
+    nc, L = dA_cumsum.shape[2], dA_cumsum.shape[3]
+    n = C.shape[-1]
+    head_group = torch.arange(h) // (h // n_groups)
+    Ch = C.float().reshape(b, nc, L, n_groups, n)[:, :, :, head_group, :]   # B NC L H N
+    dA = dA_cumsum.float()                                                  # B H NC L
+    hist = torch.einsum("bclhn,bchpn->bclhp", Ch, prev_states.float())
+    hist = hist * torch.exp(dA.permute(0, 2, 3, 1)).unsqueeze(-1)
+    causal = torch.tril(torch.ones(L, L, dtype=torch.bool))
+    decay = torch.exp(dA.unsqueeze(-1) - dA.unsqueeze(-2)).masked_fill(~causal, 0.0)
+    weight = (cb.float()[:, :, head_group] * decay.permute(0, 2, 1, 3, 4)
+              * dt.float().permute(0, 2, 1, 3).unsqueeze(-2))                  # B NC H L L
+    intra = torch.einsum("bchls,bcshp->bclhp", weight, x.float().reshape(b, nc, L, h, p))
+    return (hist + intra).reshape(b, seq, h, p)

@@ -333,6 +333,38 @@ def main() -> None:
              {"source": "_gla_decode_kernel.py:golden_gla_decode", "scale": scale,
               "scale_arg": sc, "seed": SEED})
 
+    # ---- Mamba-2 SSD chunk scan: the reference kernel's golden on the input
+    # distribution of its own harness (_ssd_chunk_scan_fwd_kernel.py:686-700:
+    # x, cb, C ~ 0.1 N(0,1); dA_cumsum = -cumsum(U(0,1)) * decay; prev ~ 0.1
+    # N(0,1) fp32; dt = 0.1 U(0,1) + 0.01), drawn here on the CPU.
+    gold = src.function(K + "mamba/ssd_chunk_scan/ssd_chunk_scan_kernel/perf_opt/"
+                        "_ssd_chunk_scan_fwd_kernel.py", "golden_ssd_chunk_scan_fwd")
+    # Its L0 cases 1, 2, 4, 5 (:762-770; case 3 left out of the fixture size
+    # budget), boundary cases (:819-825) and one deep-decay case (:798-804).
+    for B_, C_, Q_, H_, P_, N_, G_, dt_, seed, decay in [
+            (1, 2, 64, 4, 64, 32, 1, torch.float16, 0, 1.0),
+            (1, 2, 128, 4, 128, 32, 1, torch.bfloat16, 1, 1.0),
+            (2, 2, 64, 4, 64, 32, 2, torch.bfloat16, 3, 1.0),
+            (1, 2, 96, 4, 48, 48, 1, torch.float16, 4, 1.0),
+            (1, 2, 80, 4, 64, 32, 1, torch.float16, 33, 1.0),
+            (1, 2, 64, 4, 64, 16, 1, torch.float16, 31, 1.0),
+            (2, 2, 128, 4, 64, 64, 2, torch.float16, 23, 100.0)]:
+        torch.manual_seed(seed)
+        S_ = C_ * Q_
+        x = torch.randn(B_, S_, H_, P_, dtype=dt_) * 0.1
+        cb = torch.randn(B_, C_, G_, Q_, Q_, dtype=dt_) * 0.1
+        dA = -torch.rand(B_, H_, C_, Q_, dtype=torch.float32).cumsum(-1) * decay
+        Cm = torch.randn(B_, S_, G_, N_, dtype=dt_) * 0.1
+        prev = torch.randn(B_, C_, H_, P_, N_, dtype=torch.float32) * 0.1
+        dtt = torch.rand(B_, H_, C_, Q_, dtype=dt_) * 0.1 + 0.01
+        out = gold(x, cb, dA, Cm, prev, dtt, G_)
+        save(f"ssd_chunk_scan_b{B_}_c{C_}_q{Q_}_h{H_}_p{P_}_n{N_}_g{G_}_{dn[dt_]}"
+             + ("_deep" if decay != 1.0 else ""),
+             {"x": x, "cb": cb, "dA_cumsum": dA, "C": Cm, "prev_states": prev, "dt": dtt},
+             {"out": out},
+             {"source": "_ssd_chunk_scan_fwd_kernel.py:golden_ssd_chunk_scan_fwd",
+              "n_groups": G_, "seed": seed, "decay_scale": decay})
+
 
 if __name__ == "__main__":
     main()

@@ -151,3 +151,12 @@ def test_oracle_gla_decode(name):
     o, ns = ref.gla_decode(i["q"], i["k"], i["v"], i["gk"], i["state"], m["scale"])
     assert_same(o, case["outputs"]["o"])
     assert_same(ns, case["outputs"]["new_state"])
+
+
+@pytest.mark.parametrize("name", names("ssd_chunk_scan_"))
+def test_oracle_ssd_chunk_scan(name):
+    case = load(name)
+    i, m = case["inputs"], case["meta"]
+    out = ref.ssd_chunk_scan(i["x"], i["cb"], i["dA_cumsum"], i["C"], i["prev_states"], i["dt"],
+                             m["n_groups"])
+    torch.testing.assert_close(out, case["outputs"]["out"], atol=1e-6, rtol=1e-5)

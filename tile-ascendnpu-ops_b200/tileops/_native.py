@@ -82,6 +82,7 @@ _SIGNATURES: dict[str, list] = {
     "tileops_gdn_varlen_workspace_bytes": [_i64] * 5,
     "tileops_gdn_prefill_varlen_fwd": [_p] * 6 + [_i64] + [_p] * 4 + [_i64] * 5 + [_d, _i, _i, _p],
     "tileops_gla_decode_fwd": [_p] * 7 + [_i64] * 4 + [_d, _i, _p],
+    "tileops_ssd_chunk_scan_fwd": [_p] * 7 + [_i64] * 7 + [_i, _p],
     "tileops_device_error_flag": [_p, _i],
     "tileops_abi_version": [],
     "tileops_status_string": [_i],
