@@ -12,8 +12,8 @@
 // and kernels/mamba/ssd_chunk_scan/ssd_chunk_scan_kernel/perf_opt/
 // _ssd_chunk_scan_fwd_kernel.py:181 (golden at :123-178).
 //
-// One CTA (128 threads) per (b, c, h, 128-row tile of the chunk); thread r
-// owns row l0 + r (TMEM lane r).  Both terms are tcgen05 MMAs (M = 128,
+// One CTA (256 threads, two per SM) per (b, c, h, 128-row tile of the
+// chunk); row l0 + r of the tile is TMEM lane r.  Both terms are tcgen05 MMAs (M = 128,
 // N = P, kind::f16, fp32 accumulators in TMEM):
 //   D1 = C_tile [128 x N] . prev^T        A K-major (C rows), B K-major (prev
 //                                          rows p, converted fp32 -> dtype)
@@ -21,8 +21,9 @@
 //                                          registers, B MN-major (x rows s)
 // with W[l, s] = cb[l, s] exp(dA[l] - dA[s]) dt[s] for s <= l (< Q), else 0.
 // Operands are staged with cp.async (16-byte copies, zero fill past the
-// chunk / past N) into 128-byte-swizzled shared tiles; the W and x blocks are
-// double-buffered so block j+1 is built while the tensor core runs block j.
+// chunk / past N) into 128-byte-swizzled shared tiles; W blocks are double-
+// and x blocks triple-buffered: the x rows of block j+1 are requested while
+// block j's W is built and its MMAs run.
 // Epilogue: out = exp(dA[l]) D1 + D2 straight from TMEM to global fp32.
 // Every mbarrier wait is bounded (2 s); a timeout sets the device error flag,
 // the MMAs issued so far are drained and TMEM is freed before returning.
@@ -36,7 +37,8 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kSsdThreads = 128;
+constexpr int kSsdThreads = 256;
+constexpr int kSsdRowGroups = kSsdThreads / 8;  // rows of a W block handled together
 constexpr int kSsdRows = 128;   // chunk rows per CTA (MMA M)
 constexpr int kSsdKBlk = 64;    // keys per W / x block
 constexpr int kSsdMaxN = 256;   // d_state
@@ -48,17 +50,28 @@ __device__ __forceinline__ uint32_t ssd_swz(int r, int u) {
   return static_cast<uint32_t>(r * 128 + ((u ^ (r & 7)) << 4));
 }
 
-struct SsdSmem {
-  static constexpr int kC = 0;                                     // [128][256] K-major
-  static constexpr int kPrev = kC + kSsdRows * kSsdMaxN * 2;       // [P][256] K-major
-  static constexpr int kW = kPrev + kSsdMaxP * kSsdMaxN * 2;       // 2 x [128][64]
-  static constexpr int kX = kW + 2 * kSsdRows * kSsdKBlk * 2;      // 2 x [64][128] MN-major
-  static constexpr int kDA = kX + 2 * kSsdKBlk * kSsdMaxP * 2;     // Q floats
-  static constexpr int kDt = kDA + kSsdMaxQ * 4;                   // Q floats
-  static constexpr int kBar = kDt + kSsdMaxQ * 4;                  // mbarriers, tmem base
-  static constexpr int kBytes = kBar + 64;
-  static constexpr int kAlloc = kBytes + 1024;
-  static_assert(kAlloc <= 232448, "SSD shared memory exceeds 227 KB");
+// Shared-memory layout, sized per call (offsets in bytes from a 1 KB-aligned
+// base, every tile 1 KB aligned): C [128][nc64] and prev [P][nc64] K-major
+// (nc64 = d_state rounded up to 64-column chunks), two W blocks [128][64],
+// three x blocks [64][pc64] MN-major (pc64 = d_head rounded up to 64), dA and
+// dt of the chunk, the barriers.
+struct SsdLayout {
+  int c, prev, w, x, da, dt, rng, bar, bytes;
+  int x_stride;  // bytes of one x block
+  __host__ __device__ static int up1k(int v) { return (v + 1023) & ~1023; }
+  __host__ __device__ SsdLayout(int P, int N, int Q) {
+    const int nc64 = ((N + 63) / 64) * 64, pc64 = ((P + 63) / 64) * 64;
+    c = 0;
+    prev = up1k(c + kSsdRows * nc64 * 2);
+    w = up1k(prev + P * nc64 * 2);
+    x = w + 2 * kSsdRows * kSsdKBlk * 2;
+    x_stride = kSsdKBlk * pc64 * 2;
+    da = up1k(x + 3 * x_stride);
+    dt = da + Q * 4;
+    rng = dt + Q * 4;  // per 64-key block: min, max of dA (2 x 16 floats)
+    bar = up1k(rng + 2 * 16 * 4);
+    bytes = bar + 64;
+  }
 };
 
 struct SsdBars {
@@ -73,8 +86,15 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool v
                "r"(valid ? 16 : 0)
                : "memory");
 }
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
 __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.wait_all;" ::: "memory");
+}
+// Every committed group but the most recent one has completed.
+__device__ __forceinline__ void cp_async_wait_prev() {
+  asm volatile("cp.async.wait_group 1;" ::: "memory");
 }
 
 template <typename T>
@@ -100,19 +120,22 @@ struct SsdParams {
   float* out;
   int B, NC, Q, H, P, N, G;
   int ltiles;  // ceil(Q / 128)
+  FastDivU32 div_c;  // npad / 8: 16-byte units of a C / prev row
+  FastDivU32 div_x;  // P / 8: 16-byte units of an x row
+  FastDivU32 div_o;  // P / 4: 16-byte units of an fp32 output row
   int* err;
 };
 
 template <typename T>
-__global__ void __launch_bounds__(kSsdThreads, 1) ssd_chunk_scan(const SsdParams p) {
-  using L = SsdSmem;
+__global__ void __launch_bounds__(kSsdThreads, 2) ssd_chunk_scan(const SsdParams p) {
+  const SsdLayout L(p.P, p.N, p.Q);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  SsdBars* bars = reinterpret_cast<SsdBars*>(sm + L::kBar);
+  SsdBars* bars = reinterpret_cast<SsdBars*>(sm + L.bar);
   volatile int* abort_flag = &bars->abort_flag;
-  float* sdA = reinterpret_cast<float*>(sm + L::kDA);
-  float* sdt = reinterpret_cast<float*>(sm + L::kDt);
+  float* sdA = reinterpret_cast<float*>(sm + L.da);
+  float* sdt = reinterpret_cast<float*>(sm + L.dt);
   const uint32_t sb = smem_u32(sm);
   const int tid = threadIdx.x, warp = tid >> 5;
 
@@ -139,8 +162,10 @@ __global__ void __launch_bounds__(kSsdThreads, 1) ssd_chunk_scan(const SsdParams
     bars->abort_flag = 0;
     fence_mbar_init();
   }
+  // TMEM: D1 at column 0, D2 at column P rounded up to 64.
+  const uint32_t tmem_cols = ((P + 63) & ~63) * 2 <= 128 ? 128u : 256u;
   if (warp == 0) {
-    tmem_alloc(&bars->tmem_base, 256);
+    tmem_alloc(&bars->tmem_base, tmem_cols);
     tmem_relinquish();
   }
 
@@ -151,141 +176,207 @@ __global__ void __launch_bounds__(kSsdThreads, 1) ssd_chunk_scan(const SsdParams
     sdt[i] = Cvt<T>::to_f(static_cast<const T*>(p.dt)[hc * Q + i]);
   }
 
-  // ---- C tile (rows l0.., n < npad) by cp.async, zero past the chunk / N
-  {
-    const T* Cg = static_cast<const T*>(p.C);
-    const int upr = npad / 8;  // 16-byte units per row
-    for (int i = tid; i < kSsdRows * upr; i += kSsdThreads) {
-      const int r = i / upr, u = i - r * upr;
-      const int l = l0 + r, n = u * 8;
-      const bool ok = l < Q && n < N;
-      const T* src = Cg + ((static_cast<int64_t>(b) * S + c * Q + (ok ? l : 0)) * p.G + g) * N +
-                     (ok ? n : 0);
-      cp_async16(sb + L::kC + (n >> 6) * (kSsdRows * 128) + ssd_swz(r, (n & 63) >> 3), src, ok);
-    }
-  }
-  // ---- prev (P x N fp32) -> dtype, K-major [p][n]
-  {
-    const float* pg = p.prev + ((static_cast<int64_t>(b) * p.NC + c) * p.H + h) * P * N;
-    const int upr = npad / 8;
-    for (int i = tid; i < P * upr; i += kSsdThreads) {
-      const int r = i / upr, u = i - r * upr, n = u * 8;
-      uint4 pk = make_uint4(0u, 0u, 0u, 0u);
-      if (n < N) {
-        const float4 a = *reinterpret_cast<const float4*>(pg + static_cast<int64_t>(r) * N + n);
-        const float4 d = *reinterpret_cast<const float4*>(pg + static_cast<int64_t>(r) * N + n + 4);
-        pk.x = pack16<T>(a.x, a.y);
-        pk.y = pack16<T>(a.z, a.w);
-        pk.z = pack16<T>(d.x, d.y);
-        pk.w = pack16<T>(d.z, d.w);
-      }
-      *reinterpret_cast<uint4*>(sm + L::kPrev + (n >> 6) * (P * 128) + ssd_swz(r, (n & 63) >> 3)) =
-          pk;
-    }
-  }
-  __syncthreads();  // sdA / sdt visible
-
-  // W and x of key block j into buffer j & 1.
   const T* xg = static_cast<const T*>(p.x);
   const T* cbg = static_cast<const T*>(p.cb) +
                  ((static_cast<int64_t>(b) * p.NC + c) * p.G + g) * static_cast<int64_t>(Q) * Q;
-  auto stage = [&](int j) {
-    const int buf = j & 1;
-    const int s0 = j * kSsdKBlk;
-    // x rows s0.. (MN-major, P columns in 64-wide chunks)
-    const int upr = P / 8;
+  // Thread layout of a W block: packet column cpk (keys 8 cpk.. of the
+  // block) of rows rg + kSsdRowGroups it.
+  const int cpk = tid & 7, rg = tid >> 3;
+  const bool cbvec = (Q & 7) == 0;
+  uint4 cbr[kSsdRows / kSsdRowGroups];  // this thread's cb packets of the next W block
+  auto load_cb = [&](int j) {  // global -> registers, all eight in flight
+    const int sc = j * kSsdKBlk + cpk * 8;
+#pragma unroll
+    for (int it = 0; it < kSsdRows / kSsdRowGroups; ++it) {
+      const int l = l0 + rg + kSsdRowGroups * it;
+      cbr[it] = make_uint4(0u, 0u, 0u, 0u);
+      if (l < Q && sc <= l) {
+        const T* row = cbg + static_cast<int64_t>(l) * Q + sc;
+        if (cbvec && sc + 8 <= Q) {
+          cbr[it] = __ldg(reinterpret_cast<const uint4*>(row));
+        } else {
+          T* cv = reinterpret_cast<T*>(&cbr[it]);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) cv[e] = sc + e < Q ? row[e] : Cvt<T>::from_f(0.0f);
+        }
+      }
+    }
+  };
+  auto issue_x = [&](int j) {  // x rows of key block j -> buffer j % 3 (cp.async)
+    const int s0 = j * kSsdKBlk, upr = P / 8;
     for (int i = tid; i < kSsdKBlk * upr; i += kSsdThreads) {
-      const int r = i / upr, u = i - r * upr;
+      const int r = static_cast<int>(p.div_x.div(i)), u = i - r * upr;
       const int s = s0 + r, pc = u * 8;
       const bool ok = s < Q;
       const T* src = xg + ((static_cast<int64_t>(b) * S + c * Q + (ok ? s : 0)) * p.H + h) * P + pc;
-      cp_async16(sb + L::kX + buf * (kSsdKBlk * kSsdMaxP * 2) + (pc >> 6) * (kSsdKBlk * 128) +
+      cp_async16(sb + L.x + (j % 3) * L.x_stride + (pc >> 6) * (kSsdKBlk * 128) +
                      ssd_swz(r, (pc & 63) >> 3),
                  src, ok);
     }
-    // W rows (thread: packet column tid & 7 = keys s0 + 8 (tid & 7).., rows tid >> 3 + 16 i)
-    const int cp = tid & 7, rg = tid >> 3;
-    const int sc = s0 + cp * 8;
+  };
+  auto build_w = [&](int j) {  // W block j from cbr -> buffer j & 1
+    const int s0 = j * kSsdKBlk, sc = s0 + cpk * 8;
+    // exp(dA_l - dA_s) = exp(dA_l - ref) exp(ref - dA_s) with ref = dA[s0]
+    // when every exponent of the block (its keys, this tile's rows) stays
+    // within +-60 (both factors normal fp32 numbers); else per entry.
+    const float ref = sdA[s0];
+    const float* rng = reinterpret_cast<const float*>(sm + L.rng);
+    const int r0 = l0 / kSsdKBlk, r1 = min(r0 + 1, (Q - 1) / kSsdKBlk);
+    const float lo = fminf(fminf(rng[j], rng[r0]), rng[r1]);
+    const float hi = fmaxf(fmaxf(rng[16 + j], rng[16 + r0]), rng[16 + r1]);
+    const bool fact = hi - ref <= 60.0f && ref - lo <= 60.0f;
     float das[8], dts[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       const int s = sc + e;
-      das[e] = s < Q ? sdA[s] : 0.0f;
+      das[e] = s < Q ? sdA[s] : ref;
       dts[e] = s < Q ? sdt[s] : 0.0f;
+      if (fact) dts[e] *= __expf(ref - das[e]);  // exp(ref - dA_s) dt_s
     }
-    const bool vec = (Q & 7) == 0;
-#pragma unroll 2
-    for (int it = 0; it < kSsdRows / 16; ++it) {
-      const int r = rg + 16 * it;
+#pragma unroll
+    for (int it = 0; it < kSsdRows / kSsdRowGroups; ++it) {
+      const int r = rg + kSsdRowGroups * it;
       const int l = l0 + r;
       float w[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) w[e] = 0.0f;
-      if (l < Q && sc <= l) {
-        T cv[8];
-        const T* row = cbg + static_cast<int64_t>(l) * Q + sc;
-        if (vec && sc + 8 <= Q) {
-          *reinterpret_cast<uint4*>(cv) = *reinterpret_cast<const uint4*>(row);
-        } else {
-#pragma unroll
-          for (int e = 0; e < 8; ++e) cv[e] = sc + e < Q ? row[e] : Cvt<T>::from_f(0.0f);
-        }
-        const float dal = sdA[l];
+      const T* cv = reinterpret_cast<const T*>(&cbr[it]);
+      const float dal = l < Q ? sdA[l] : ref;
+      if (fact) {
+        const float el = __expf(dal - ref);
 #pragma unroll
         for (int e = 0; e < 8; ++e)
-          if (sc + e <= l) w[e] = Cvt<T>::to_f(cv[e]) * __expf(dal - das[e]) * dts[e];
+          w[e] = (l < Q && sc + e <= l) ? Cvt<T>::to_f(cv[e]) * el * dts[e] : 0.0f;
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          w[e] = (l < Q && sc + e <= l) ? Cvt<T>::to_f(cv[e]) * __expf(dal - das[e]) * dts[e]
+                                        : 0.0f;
       }
       uint4 pk;
       pk.x = pack16<T>(w[0], w[1]);
       pk.y = pack16<T>(w[2], w[3]);
       pk.z = pack16<T>(w[4], w[5]);
       pk.w = pack16<T>(w[6], w[7]);
-      *reinterpret_cast<uint4*>(sm + L::kW + buf * (kSsdRows * 128) + ssd_swz(r, cp)) = pk;
+      *reinterpret_cast<uint4*>(sm + L.w + (j & 1) * (kSsdRows * 128) + ssd_swz(r, cpk)) = pk;
     }
   };
+
+  // ---- prologue: x and C of block 0 (cp.async), cb rows of block 0 and prev
+  // (registers) all in flight together
+  issue_x(0);
+  {
+    const T* Cg = static_cast<const T*>(p.C);
+    const int upr = npad / 8;  // 16-byte units per row
+    for (int i = tid; i < kSsdRows * upr; i += kSsdThreads) {
+      const int r = static_cast<int>(p.div_c.div(i)), u = i - r * upr;
+      const int l = l0 + r, n = u * 8;
+      const bool ok = l < Q && n < N;
+      const T* src = Cg + ((static_cast<int64_t>(b) * S + c * Q + (ok ? l : 0)) * p.G + g) * N +
+                     (ok ? n : 0);
+      cp_async16(sb + L.c + (n >> 6) * (kSsdRows * 128) + ssd_swz(r, (n & 63) >> 3), src, ok);
+    }
+  }
+  cp_async_commit();  // group: x block 0 and the C tile
+  load_cb(0);
+  {
+    // prev (P x N fp32) -> dtype, K-major [p][n]; eight packets per thread
+    // loaded before any is converted.
+    const float* pg = p.prev + ((static_cast<int64_t>(b) * p.NC + c) * p.H + h) * P * N;
+    const int upr = npad / 8, total = P * upr;
+    for (int base = 0; base < total; base += 8 * kSsdThreads) {
+      float4 va[8], vb[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int i = base + k * kSsdThreads + tid;
+        va[k] = vb[k] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (i < total) {
+          const int r = static_cast<int>(p.div_c.div(i)), n = (i - r * upr) * 8;
+          if (n < N) {
+            const float* src = pg + static_cast<int64_t>(r) * N + n;
+            va[k] = __ldcs(reinterpret_cast<const float4*>(src));
+            vb[k] = __ldcs(reinterpret_cast<const float4*>(src + 4));
+          }
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int i = base + k * kSsdThreads + tid;
+        if (i < total) {
+          const int r = static_cast<int>(p.div_c.div(i)), n = (i - r * upr) * 8;
+          uint4 pk;
+          pk.x = pack16<T>(va[k].x, va[k].y);
+          pk.y = pack16<T>(va[k].z, va[k].w);
+          pk.z = pack16<T>(vb[k].x, vb[k].y);
+          pk.w = pack16<T>(vb[k].z, vb[k].w);
+          *reinterpret_cast<uint4*>(sm + L.prev + (n >> 6) * (P * 128) +
+                                    ssd_swz(r, (n & 63) >> 3)) = pk;
+        }
+      }
+    }
+  }
+  __syncthreads();  // sdA / sdt visible
+  {
+    // min / max of dA over each 64-key block (warp w: blocks w, w + 4, ...)
+    float* rng = reinterpret_cast<float*>(sm + L.rng);
+    const int lane = tid & 31;
+    for (int jb = warp; jb * kSsdKBlk < Q; jb += kSsdThreads / 32) {
+      float mn = INFINITY, mx = -INFINITY;
+      for (int k = lane; k < kSsdKBlk; k += 32) {
+        const int s = jb * kSsdKBlk + k;
+        if (s < Q) {
+          mn = fminf(mn, sdA[s]);
+          mx = fmaxf(mx, sdA[s]);
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      }
+      if (lane == 0) {
+        rng[jb] = mn;
+        rng[16 + jb] = mx;
+      }
+    }
+  }
+  __syncthreads();
 
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   const uint32_t id_kk = idesc_f16_major(kSsdRows, P, kBf16 ? 1 : 0, 0, 0);
   const uint32_t id_kmn = idesc_f16_major(kSsdRows, P, kBf16 ? 1 : 0, 0, 1);
-  stage(0);
-  cp_async_wait_all();
-  fence_proxy_async_smem();
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
-  const uint32_t t_d1 = tmem, t_d2 = tmem + 128;
+  const uint32_t p64 = static_cast<uint32_t>((P + 63) & ~63);
+  const uint32_t t_d1 = tmem, t_d2 = tmem + p64;
   bool ok = true;
   int issued = 0;  // key blocks whose MMAs were issued
   for (int j = 0; j < nblk; ++j) {
     const int buf = j & 1;
-    if (j > 0) {
-      // Buffer `buf` was last read by block j - 2's MMAs.
-      if (j >= 2 && !mbar_wait(&bars->blk_done[buf], ((j - 2) >> 1) & 1, p.err, abort_flag)) {
-        ok = false;
-      }
+    if (j >= 2) {
+      // Block j - 2's MMAs read W buffer `buf` and x buffer (j + 1) % 3.
+      if (!mbar_wait(&bars->blk_done[buf], ((j - 2) >> 1) & 1, p.err, abort_flag)) ok = false;
       if (!__syncthreads_and(ok)) {
         ok = false;
         break;
       }
-      stage(j);
-      cp_async_wait_all();
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncthreads();
-      tc_fence_after();
     }
+    if (j + 1 < nblk) issue_x(j + 1);  // one block ahead
+    cp_async_commit();
+    build_w(j);
+    if (j + 1 < nblk) load_cb(j + 1);  // in flight during this block's MMAs
+    cp_async_wait_prev();              // x of block j (and the C tile) landed
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
     if (tid == 0) {
       if (j == 0) {
-        const uint64_t a = smem_desc(sb + L::kC, 16, 1024);
-        const uint64_t bd = smem_desc(sb + L::kPrev, 16, 1024);
+        const uint64_t a = smem_desc(sb + L.c, 16, 1024);
+        const uint64_t bd = smem_desc(sb + L.prev, 16, 1024);
         for (int kk = 0; kk < npad / 16; ++kk)
           mma_f16_ss(t_d1, desc_advance(a, (kk >> 2) * (kSsdRows * 128) + (kk & 3) * 32),
                      desc_advance(bd, (kk >> 2) * (P * 128) + (kk & 3) * 32), id_kk, kk > 0);
       }
-      const uint64_t a = smem_desc(sb + L::kW + buf * (kSsdRows * 128), 16, 1024);
-      const uint64_t bd =
-          smem_desc(sb + L::kX + buf * (kSsdKBlk * kSsdMaxP * 2), kSsdKBlk * 128, 1024);
+      const uint64_t a = smem_desc(sb + L.w + buf * (kSsdRows * 128), 16, 1024);
+      const uint64_t bd = smem_desc(sb + L.x + (j % 3) * L.x_stride, kSsdKBlk * 128, 1024);
 #pragma unroll
       for (int kk = 0; kk < kSsdKBlk / 16; ++kk)
         mma_f16_ss(t_d2, desc_advance(a, kk * 32), desc_advance(bd, kk * 16 * 128), id_kmn,
@@ -294,50 +385,71 @@ __global__ void __launch_bounds__(kSsdThreads, 1) ssd_chunk_scan(const SsdParams
     }
     issued = j + 1;
   }
+  cp_async_wait_all();  // no copy may still write this CTA's shared memory at exit
   if (tid == 0) mma_commit(&bars->all_done);
   // All threads wait for the accumulators (with a failed run: for the MMAs
   // already issued, so TMEM is not freed under them).
   const bool done = mbar_wait(&bars->all_done, 0, p.err, abort_flag, !ok);
   tc_fence_after();
-  if (ok && done && issued == nblk) {
-    const int r = tid;
+  // Uniform across the CTA: the epilogue below synchronises.
+  if (__syncthreads_and(ok && done && issued == nblk)) {
+    // out = exp(dA_l) D1 + D2, row r = TMEM lane r, staged in the freed W / x
+    // buffers as fp32 rows of P (16-byte units swizzled within groups of 8
+    // or 4), then written by consecutive threads along each row.
+    // Warps w and w + 4 share TMEM lanes 32 (w % 4).. and take alternate
+    // 32-column chunks.
+    const int r = (warp & 3) * 32 + (tid & 31);
     const int l = l0 + r;
-    const uint32_t lane = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t lane = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const float eh = l < Q ? __expf(sdA[l]) : 0.0f;
-    float* orow = p.out + ((static_cast<int64_t>(b) * S + c * Q + l) * p.H + h) * P;
-    for (int c0 = 0; c0 < P; c0 += 32) {
+    const int U = P / 4;                            // units per row
+    const int smask = (U & 7) == 0 ? 7 : 3;
+    float* stg = reinterpret_cast<float*>(sm + L.w);
+    for (int c0 = 32 * (warp >> 2); c0 < P; c0 += 64) {
       uint32_t x1[32], x2[32];
       tmem_ld32(t_d1 + lane + c0, x1);
       tmem_ld32(t_d2 + lane + c0, x2);
       tmem_wait_ld_regs(x1);
       tmem_wait_ld_regs(x2);
-      if (l < Q) {
-        const int ncol = min(32, P - c0);
-        for (int i = 0; i < ncol; i += 4)
-          *reinterpret_cast<float4*>(orow + c0 + i) =
-              make_float4(fmaf(eh, __uint_as_float(x1[i]), __uint_as_float(x2[i])),
-                          fmaf(eh, __uint_as_float(x1[i + 1]), __uint_as_float(x2[i + 1])),
-                          fmaf(eh, __uint_as_float(x1[i + 2]), __uint_as_float(x2[i + 2])),
-                          fmaf(eh, __uint_as_float(x1[i + 3]), __uint_as_float(x2[i + 3])));
+      const int ncol = min(32, P - c0);
+      for (int i = 0; i < ncol; i += 4) {
+        const int u = (c0 + i) >> 2;
+        const int us = (u & ~smask) | ((u ^ r) & smask);
+        *reinterpret_cast<float4*>(stg + r * P + us * 4) =
+            make_float4(fmaf(eh, __uint_as_float(x1[i]), __uint_as_float(x2[i])),
+                        fmaf(eh, __uint_as_float(x1[i + 1]), __uint_as_float(x2[i + 1])),
+                        fmaf(eh, __uint_as_float(x1[i + 2]), __uint_as_float(x2[i + 2])),
+                        fmaf(eh, __uint_as_float(x1[i + 3]), __uint_as_float(x2[i + 3])));
       }
+    }
+    __syncthreads();
+    const int rows = min(kSsdRows, Q - l0);
+    for (int i = tid; i < rows * U; i += kSsdThreads) {
+      const int rr = static_cast<int>(p.div_o.div(i)), u = i - rr * U;
+      const int us = (u & ~smask) | ((u ^ rr) & smask);
+      const float4 v = *reinterpret_cast<const float4*>(stg + rr * P + us * 4);
+      __stcs(reinterpret_cast<float4*>(
+                 p.out + ((static_cast<int64_t>(b) * S + c * Q + l0 + rr) * p.H + h) * P + u * 4),
+             v);
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, tmem_cols);
   }
 }
 
 template <typename T>
 int launch_ssd(const SsdParams& p, cudaStream_t s) {
   auto k = ssd_chunk_scan<T>;
-  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, SsdSmem::kAlloc) !=
-      cudaSuccess)
+  const int smem = SsdLayout(p.P, p.N, p.Q).bytes + 1024;  // + room to align the base
+  if (smem > 232448) return TILEOPS_EBADSHAPE;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return TILEOPS_ELAUNCH;
   const int64_t grid = static_cast<int64_t>(p.B) * p.NC * p.H * p.ltiles;
-  k<<<static_cast<unsigned>(grid), kSsdThreads, SsdSmem::kAlloc, s>>>(p);
+  k<<<static_cast<unsigned>(grid), kSsdThreads, smem, s>>>(p);
   return launch_status();
 }
 
@@ -384,6 +496,9 @@ extern "C" int tileops_ssd_chunk_scan_fwd(const void* x, const void* cb, const f
   p.N = static_cast<int>(d_state);
   p.G = static_cast<int>(n_groups);
   p.ltiles = static_cast<int>(ltiles);
+  p.div_c = FastDivU32(static_cast<uint32_t>(((d_state + 15) & ~15) / 8));
+  p.div_x = FastDivU32(static_cast<uint32_t>(d_head / 8));
+  p.div_o = FastDivU32(static_cast<uint32_t>(d_head / 4));
   p.err = device_error_ptr();
   cudaStream_t s = as_stream(stream);
   return dtype == TILEOPS_DT_BF16 ? launch_ssd<__nv_bfloat16>(p, s) : launch_ssd<__half>(p, s);
