@@ -171,8 +171,9 @@ __global__ void __launch_bounds__(kSsdThreads, 2) ssd_chunk_scan(const SsdParams
 
   // ---- per-chunk scalars: dA (fp32) and dt -> shared
   const int64_t hc = (static_cast<int64_t>(b) * p.H + h) * p.NC + c;
+  // dA is kept in log2 units: exp(a - b) = ex2(a' - b').
   for (int i = tid; i < Q; i += kSsdThreads) {
-    sdA[i] = p.dA[hc * Q + i];
+    sdA[i] = p.dA[hc * Q + i] * 1.4426950408889634f;
     sdt[i] = Cvt<T>::to_f(static_cast<const T*>(p.dt)[hc * Q + i]);
   }
 
@@ -214,49 +215,64 @@ __global__ void __launch_bounds__(kSsdThreads, 2) ssd_chunk_scan(const SsdParams
                  src, ok);
     }
   };
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  auto unpack2 = [](uint32_t u) -> float2 {  // a 16-bit pair -> two floats
+    if constexpr (kBf16) {
+      return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
+    } else {
+      return __half22float2(*reinterpret_cast<const __half2*>(&u));
+    }
+  };
   auto build_w = [&](int j) {  // W block j from cbr -> buffer j & 1
     const int s0 = j * kSsdKBlk, sc = s0 + cpk * 8;
     // exp(dA_l - dA_s) = exp(dA_l - ref) exp(ref - dA_s) with ref = dA[s0]
     // when every exponent of the block (its keys, this tile's rows) stays
     // within +-60 (both factors normal fp32 numbers); else per entry.
+    // (sdA is in log2 units: 60 / ln 2 = 86.56.)
     const float ref = sdA[s0];
     const float* rng = reinterpret_cast<const float*>(sm + L.rng);
     const int r0 = l0 / kSsdKBlk, r1 = min(r0 + 1, (Q - 1) / kSsdKBlk);
     const float lo = fminf(fminf(rng[j], rng[r0]), rng[r1]);
     const float hi = fmaxf(fmaxf(rng[16 + j], rng[16 + r0]), rng[16 + r1]);
-    const bool fact = hi - ref <= 60.0f && ref - lo <= 60.0f;
-    float das[8], dts[8];
+    const bool fact = hi - ref <= 86.5f && ref - lo <= 86.5f;
+    float2 das[4], dts[4];  // key pairs of this thread's packet
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const int s = sc + e;
-      das[e] = s < Q ? sdA[s] : ref;
-      dts[e] = s < Q ? sdt[s] : 0.0f;
-      if (fact) dts[e] *= __expf(ref - das[e]);  // exp(ref - dA_s) dt_s
+    for (int q = 0; q < 4; ++q) {
+      const int s = sc + 2 * q;
+      das[q] = make_float2(s < Q ? sdA[s] : ref, s + 1 < Q ? sdA[s + 1] : ref);
+      dts[q] = make_float2(s < Q ? sdt[s] : 0.0f, s + 1 < Q ? sdt[s + 1] : 0.0f);
+      if (fact)  // exp(ref - dA_s) dt_s
+        dts[q] = fmul2(dts[q], make_float2(ex2(ref - das[q].x), ex2(ref - das[q].y)));
     }
 #pragma unroll
     for (int it = 0; it < kSsdRows / kSsdRowGroups; ++it) {
       const int r = rg + kSsdRowGroups * it;
       const int l = l0 + r;
-      float w[8];
-      const T* cv = reinterpret_cast<const T*>(&cbr[it]);
+      const uint32_t* cw = reinterpret_cast<const uint32_t*>(&cbr[it]);
       const float dal = l < Q ? sdA[l] : ref;
-      if (fact) {
-        const float el = __expf(dal - ref);
+      // Rows whose whole packet is visible (l < Q, every key <= l) skip the mask.
+      const bool full = l < Q && sc + 7 <= l;
+      const float el = fact ? ex2(dal - ref) : 0.0f;
+      uint32_t pk[4];
 #pragma unroll
-        for (int e = 0; e < 8; ++e)
-          w[e] = (l < Q && sc + e <= l) ? Cvt<T>::to_f(cv[e]) * el * dts[e] : 0.0f;
-      } else {
-#pragma unroll
-        for (int e = 0; e < 8; ++e)
-          w[e] = (l < Q && sc + e <= l) ? Cvt<T>::to_f(cv[e]) * __expf(dal - das[e]) * dts[e]
-                                        : 0.0f;
+      for (int q = 0; q < 4; ++q) {
+        float2 e2;
+        if (fact) {
+          e2 = make_float2(el, el);
+        } else {
+          const float2 a = fadd2(make_float2(dal, dal), make_float2(-das[q].x, -das[q].y));
+          e2 = make_float2(ex2(a.x), ex2(a.y));
+        }
+        float2 w2 = fmul2(fmul2(unpack2(cw[q]), e2), dts[q]);
+        if (!full) {
+          const int s = sc + 2 * q;
+          w2.x = (l < Q && s <= l) ? w2.x : 0.0f;
+          w2.y = (l < Q && s + 1 <= l) ? w2.y : 0.0f;
+        }
+        pk[q] = pack16<T>(w2.x, w2.y);
       }
-      uint4 pk;
-      pk.x = pack16<T>(w[0], w[1]);
-      pk.y = pack16<T>(w[2], w[3]);
-      pk.z = pack16<T>(w[4], w[5]);
-      pk.w = pack16<T>(w[6], w[7]);
-      *reinterpret_cast<uint4*>(sm + L.w + (j & 1) * (kSsdRows * 128) + ssd_swz(r, cpk)) = pk;
+      *reinterpret_cast<uint4*>(sm + L.w + (j & 1) * (kSsdRows * 128) + ssd_swz(r, cpk)) =
+          make_uint4(pk[0], pk[1], pk[2], pk[3]);
     }
   };
 
@@ -340,7 +356,6 @@ __global__ void __launch_bounds__(kSsdThreads, 2) ssd_chunk_scan(const SsdParams
   }
   __syncthreads();
 
-  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   const uint32_t id_kk = idesc_f16_major(kSsdRows, P, kBf16 ? 1 : 0, 0, 0);
   const uint32_t id_kmn = idesc_f16_major(kSsdRows, P, kBf16 ? 1 : 0, 0, 1);
   const uint32_t tmem = bars->tmem_base;
@@ -401,7 +416,7 @@ __global__ void __launch_bounds__(kSsdThreads, 2) ssd_chunk_scan(const SsdParams
     const int r = (warp & 3) * 32 + (tid & 31);
     const int l = l0 + r;
     const uint32_t lane = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const float eh = l < Q ? __expf(sdA[l]) : 0.0f;
+    const float eh = l < Q ? ex2(sdA[l]) : 0.0f;
     const int U = P / 4;                            // units per row
     const int smask = (U & 7) == 0 ? 7 : 3;
     float* stg = reinterpret_cast<float*>(sm + L.w);
