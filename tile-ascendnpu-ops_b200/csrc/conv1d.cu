@@ -20,10 +20,21 @@
 // outputs is staged in shared memory as fp32 and each thread produces
 // outputs strided by the block size (bank-conflict free).
 //
-// Direct kernel (grouped / dense conv1d, the non-depthwise kernels of
-// kernels/convolution/conv1d/conv1d.py:152-516): one output per thread,
-// fp32 accumulation over c_in/groups * k taps.
+// Dense / grouped conv1d (the non-depthwise kernels of
+// kernels/convolution/conv1d/conv1d.py:152-516), fp16 / bf16: an implicit
+// GEMM on tcgen05 tensor cores.  Per (batch, group):
+//   y[co, o] = b[co] + sum_r W[co, r] X[r, o],   r = ci * K + k,
+//   X[r, o] = x[ci, o * stride + k * dil - pad_left]   (0 outside [0, l_in))
+// M = output channels, N = output positions, K = c_in/groups * K.  One CTA
+// (256 threads) per 128 x 128 output tile: the W rows of a 64-wide slice of r
+// arrive by cp.async into a K-major swizzled tile, the matching im2col slice
+// of x is gathered by the threads into an MN-major swizzled tile (consecutive
+// threads read consecutive positions), two stages ring while one thread
+// issues the MMAs; the fp32 accumulator lives in TMEM and the epilogue adds
+// the bias and rounds once.  fp32 (and shapes beyond the grid limits) use the
+// direct kernel: one output per thread, fp32 accumulation over the taps.
 #include "common.cuh"
+#include "sm100.cuh"
 
 namespace tileops {
 namespace {
@@ -258,6 +269,281 @@ __global__ void __launch_bounds__(kDirThreads)
   }
 }
 
+// ------------------------------------------------ implicit GEMM (tcgen05)
+constexpr int kIgThreads = 256;
+constexpr int kIgM = 128, kIgN = 128, kIgK = 64;  // tile of co x o, slice of r
+constexpr int kIgStage = kIgM * kIgK * 2 + kIgK * kIgN * 2;  // A 16 KB + B 16 KB
+constexpr int kIgSmem = 2 * kIgStage + 1024 /*bias*/ + 64 /*barriers*/ + 2 * kIgK * 16 /*row tables*/;
+
+struct IgParams {
+  const void* x;
+  const void* w;
+  const void* bias;
+  void* y;
+  int64_t c_in, l_in, c_out, l_out;
+  int K, stride, pad_left, dil, groups;
+  int cig, cog, R;  // channels per group, reduction length cig * K
+  bool w_vec;       // W rows are 16-byte multiples and aligned: cp.async path
+  FastDivU32 div_k;
+  int* err;
+};
+
+__device__ __forceinline__ uint32_t ig_swz(int r, int u) {
+  return static_cast<uint32_t>(r * 128 + ((u ^ (r & 7)) << 4));
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kIgThreads) conv1d_igemm(const IgParams p) {
+  using namespace sm100;
+  extern __shared__ uint8_t ig_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(ig_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  float* sbias = reinterpret_cast<float*>(sm + 2 * kIgStage);
+  uint64_t* done = reinterpret_cast<uint64_t*>(sm + 2 * kIgStage + 1024);  // [2]
+  uint64_t* all_done = done + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(all_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // Per stage: for the 64 reduction rows of the slice, the x offset of the
+  // channel (ci * l_in) and the tap shift k * dil, or -1 past the end.
+  int64_t* rtab = reinterpret_cast<int64_t*>(sm + 2 * kIgStage + 1024 + 64);  // [2][64][2]
+  const uint32_t sb = smem_u32(sm);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int o0 = blockIdx.x * kIgN, co0 = blockIdx.y * kIgM;
+  const int g = blockIdx.z % p.groups;
+  const int64_t b = blockIdx.z / p.groups;
+  const T* xg = static_cast<const T*>(p.x) + (b * p.c_in + static_cast<int64_t>(g) * p.cig) * p.l_in;
+  const T* wg = static_cast<const T*>(p.w) + (static_cast<int64_t>(g) * p.cog + co0) * p.R;
+  const int nchunk = (p.R + kIgK - 1) / kIgK;
+
+  if (tid == 0) {
+    mbar_init(&done[0], 1);
+    mbar_init(&done[1], 1);
+    mbar_init(all_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, 128);
+    tmem_relinquish();
+  }
+  if (tid < kIgM) {
+    const int co = co0 + tid;
+    sbias[tid] = (p.bias && co < p.cog)
+                     ? Cvt<T>::to_f(static_cast<const T*>(p.bias)[static_cast<int64_t>(g) * p.cog + co])
+                     : 0.0f;
+  }
+
+  // Slice c of r into stage c & 1: A = W[co0.., r0..] (K-major), B = X[r0.., o0..]
+  // (MN-major, 64-position chunks 8 KB apart).
+  auto stage = [&](int c) {
+    uint8_t* st = sm + (c & 1) * kIgStage;
+    const uint32_t sa = sb + (c & 1) * kIgStage;
+    const int r0 = c * kIgK;
+    if (p.w_vec) {
+      for (int i = tid; i < kIgM * 8; i += kIgThreads) {
+        const int row = i >> 3, u = i & 7;
+        const int r = r0 + u * 8;
+        const bool ok = co0 + row < p.cog && r < p.R;
+        const T* src = ok ? wg + static_cast<int64_t>(row) * p.R + r : wg;
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(sa + ig_swz(row, u)),
+                     "l"(src), "r"(ok ? 16 : 0)
+                     : "memory");
+      }
+    } else {
+      // Element path: loads in batches of 8 in flight before their stores.
+      constexpr int kPer = kIgM * kIgK / kIgThreads;
+#pragma unroll 1
+      for (int q0 = 0; q0 < kPer; q0 += 8) {
+        T v[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const int i = tid + (q0 + q) * kIgThreads;
+          const int row = i >> 6, r = r0 + (i & 63);
+          v[q] = (co0 + row < p.cog && r < p.R) ? wg[static_cast<int64_t>(row) * p.R + r]
+                                                : Cvt<T>::from_f(0.0f);
+        }
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const int i = tid + (q0 + q) * kIgThreads;
+          const int row = i >> 6, col = i & 63;
+          *reinterpret_cast<T*>(st + ig_swz(row, col >> 3) + (col & 7) * 2) = v[q];
+        }
+      }
+    }
+    // B: thread -> position o0 + (tid & 127), rows rr = tid >> 7, + 2, ...
+    // (the row table of this stage was written before the barrier that
+    // preceded this call)
+    const int64_t* tb = rtab + (c & 1) * kIgK * 2;
+    uint8_t* bt = st + kIgM * kIgK * 2;
+    const int oo = tid & (kIgN - 1);
+    const int64_t pos0 = static_cast<int64_t>(o0 + oo) * p.stride - p.pad_left;
+    const bool o_ok = o0 + oo < p.l_out;
+    uint8_t* bcol = bt + (oo >> 6) * (kIgK * 128) + (oo & 7) * 2;
+    const int ucol = (oo & 63) >> 3;
+    // This thread's kRows gather loads, in batches of 16 in flight before
+    // their stores.
+    constexpr int kRows = kIgK * kIgN / kIgThreads;
+#pragma unroll 1
+    for (int q0 = 0; q0 < kRows; q0 += 16) {
+      T v[16];
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        const int rr = (tid >> 7) + (q0 + q) * (kIgThreads / kIgN);
+        const int64_t coff = tb[2 * rr], shift = tb[2 * rr + 1];  // warp-uniform
+        const int64_t pos = pos0 + shift;
+        v[q] = (coff >= 0 && o_ok && pos >= 0 && pos < p.l_in) ? xg[coff + pos]
+                                                               : Cvt<T>::from_f(0.0f);
+      }
+#pragma unroll
+      for (int q = 0; q < 16; ++q)
+        *reinterpret_cast<T*>(bcol + ig_swz((tid >> 7) + (q0 + q) * (kIgThreads / kIgN), ucol)) =
+            v[q];
+    }
+  };
+
+  auto write_table = [&](int c) {  // threads 0..63: row table of slice c
+    if (tid < kIgK) {
+      const int r = c * kIgK + tid;
+      int64_t* t = rtab + (c & 1) * kIgK * 2 + 2 * tid;
+      if (r < p.R) {
+        const int ci = static_cast<int>(p.div_k.div(static_cast<uint32_t>(r)));
+        t[0] = static_cast<int64_t>(ci) * p.l_in;
+        t[1] = static_cast<int64_t>(r - ci * p.K) * p.dil;
+      } else {
+        t[0] = -1;
+        t[1] = 0;
+      }
+    }
+  };
+  write_table(0);
+  if (nchunk > 1) write_table(1);
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  const uint32_t idesc = idesc_f16_major(kIgM, kIgN, kBf16 ? 1 : 0, 0, 1);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  bool ok = true;
+  int issued = 0;
+  for (int c = 0; c < nchunk; ++c) {
+    const int buf = c & 1;
+    if (c >= 2) {  // stage `buf` was read by slice c - 2's MMAs
+      if (!mbar_wait(&done[buf], ((c - 2) >> 1) & 1, p.err, abort_flag)) ok = false;
+      if (!__syncthreads_and(ok)) {
+        ok = false;
+        break;
+      }
+    }
+    stage(c);
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    // Every thread is past stage(c): its table slot takes slice c + 2 (read
+    // only after the barrier at the top of iteration c + 2).
+    if (c + 2 < nchunk) write_table(c + 2);
+    if (tid == 0) {
+      const uint64_t a = smem_desc(sb + buf * kIgStage, 16, 1024);
+      const uint64_t bd = smem_desc(sb + buf * kIgStage + kIgM * kIgK * 2, kIgK * 128, 1024);
+#pragma unroll
+      for (int kk = 0; kk < kIgK / 16; ++kk)
+        mma_f16_ss(tmem, desc_advance(a, kk * 32), desc_advance(bd, kk * 16 * 128), idesc,
+                   (c > 0 || kk > 0) ? 1u : 0u);
+      mma_commit(&done[buf]);
+    }
+    issued = c + 1;
+  }
+  if (tid == 0) mma_commit(all_done);
+  const bool fin = mbar_wait(all_done, 0, p.err, abort_flag, !ok);
+  tc_fence_after();
+  // Uniform across the CTA: the epilogue below synchronises.
+  if (__syncthreads_and(ok && fin && issued == nchunk)) {
+    // TMEM lane = output channel co0 + 32 (w % 4) + lane; warps w and w + 4
+    // take positions [0, 64) and [64, 128).  The rounded tile is staged in
+    // the freed stage buffers as [128 co][128 o] (16-byte units swizzled by
+    // row) and written row by row by consecutive threads, coalesced whatever
+    // the alignment of the rows in y.
+    const int row = (warp & 3) * 32 + (tid & 31);
+    const int cb = (warp >> 2) * 64;
+    const uint32_t lane = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const float bv = sbias[row];
+    uint8_t* stg = sm;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint32_t v[32];
+      tmem_ld32(tmem + lane + cb + h * 32, v);
+      tmem_wait_ld_regs(v);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 pk;
+        uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const T lo = Cvt<T>::from_f(__uint_as_float(v[8 * q + 2 * e]) + bv);
+          const T hi = Cvt<T>::from_f(__uint_as_float(v[8 * q + 2 * e + 1]) + bv);
+          pw[e] = static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&lo)) |
+                  (static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&hi)) << 16);
+        }
+        const int u = (cb + h * 32) / 8 + q;  // 16-byte unit of the row (16 per row)
+        *reinterpret_cast<uint4*>(stg + row * 256 + ((u ^ (row & 15)) << 4)) = pk;
+      }
+    }
+    __syncthreads();
+    const int nrow = min(kIgM, p.cog - co0), ncol = min(kIgN, static_cast<int>(p.l_out - o0));
+    T* ybase = static_cast<T*>(p.y) +
+               (b * p.c_out + static_cast<int64_t>(g) * p.cog + co0) * p.l_out + o0;
+    for (int rr = warp; rr < nrow; rr += kIgThreads / 32) {
+      T* yr = ybase + static_cast<int64_t>(rr) * p.l_out;
+      for (int c = tid & 31; c < ncol; c += 32) {
+        const int u = c >> 3;
+        yr[c] = *reinterpret_cast<const T*>(stg + rr * 256 + ((u ^ (rr & 15)) << 4) + (c & 7) * 2);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 128);
+  }
+}
+
+template <typename T>
+int launch_igemm(const void* x, const void* w, const void* bias, void* y, int64_t n,
+                 int64_t c_in, int64_t l_in, int64_t c_out, int64_t l_out, int K, int stride,
+                 int pad_left, int dil, int64_t groups, cudaStream_t s) {
+  IgParams p;
+  p.x = x;
+  p.w = w;
+  p.bias = bias;
+  p.y = y;
+  p.c_in = c_in;
+  p.l_in = l_in;
+  p.c_out = c_out;
+  p.l_out = l_out;
+  p.K = K;
+  p.stride = stride;
+  p.pad_left = pad_left;
+  p.dil = dil;
+  p.groups = static_cast<int>(groups);
+  p.cig = static_cast<int>(c_in / groups);
+  p.cog = static_cast<int>(c_out / groups);
+  p.R = p.cig * K;
+  p.w_vec = p.R % 8 == 0 && aligned16(w);
+  p.div_k = FastDivU32(static_cast<uint32_t>(K));
+  p.err = device_error_ptr();
+  auto k = conv1d_igemm<T>;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kIgSmem + 1024) !=
+      cudaSuccess)
+    return TILEOPS_ELAUNCH;
+  const dim3 grid(static_cast<unsigned>((l_out + kIgN - 1) / kIgN),
+                  static_cast<unsigned>((p.cog + kIgM - 1) / kIgM),
+                  static_cast<unsigned>(n * groups));
+  k<<<grid, kIgThreads, kIgSmem + 1024, s>>>(p);
+  return launch_status();
+}
+
 template <typename T, typename W>
 int launch_dw_t(const void* x, const void* w, const void* bias, void* y, int64_t n, int64_t c,
                 int64_t l_in, int64_t l_out, int K, int stride, int pad_left, int dil, int act,
@@ -345,6 +631,20 @@ extern "C" int tileops_conv1d_direct_fwd(const void* x, const void* w, const voi
   if (n == 0 || l_out == 0) return TILEOPS_OK;
   if (!x || !w || !y) return TILEOPS_EINVAL;
   cudaStream_t s = as_stream(stream);
+  // 16-bit: the tcgen05 implicit GEMM when the grid and the 32-bit index
+  // arithmetic of its gather fit.
+  const int64_t cig = c_in / groups;
+  if ((dtype == TILEOPS_DT_F16 || dtype == TILEOPS_DT_BF16) && n * groups <= 65535 &&
+      (c_out / groups + kIgM - 1) / kIgM <= 65535 && (l_out + kIgN - 1) / kIgN <= 0x7fffffffLL &&
+      cig * k <= 0x7fffffffLL && l_out * stride <= (1LL << 40)) {
+    const int K = static_cast<int>(k), st = static_cast<int>(stride),
+              dl = static_cast<int>(dilation), pl = static_cast<int>(pad_left);
+    return dtype == TILEOPS_DT_BF16
+               ? launch_igemm<__nv_bfloat16>(x, w, bias, y, n, c_in, l_in, c_out, l_out, K, st,
+                                             pl, dl, groups, s)
+               : launch_igemm<__half>(x, w, bias, y, n, c_in, l_in, c_out, l_out, K, st, pl, dl,
+                                      groups, s);
+  }
   const int64_t total = n * c_out * l_out;
   const unsigned grid = stream_grid(total, kDirThreads, 16);
   const int K = static_cast<int>(k), st = static_cast<int>(stride), dl = static_cast<int>(dilation),
