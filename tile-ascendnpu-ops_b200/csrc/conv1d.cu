@@ -277,6 +277,7 @@ constexpr int kIgSmem = 2 * kIgStage + 1024 /*bias*/ + 64 /*barriers*/ + 2 * kIg
 
 struct IgParams {
   const void* x;
+  const void* x_end;  // one past the last element of x (bounds of the aligned loads)
   const void* w;
   const void* bias;
   void* y;
@@ -284,12 +285,29 @@ struct IgParams {
   int K, stride, pad_left, dil, groups;
   int cig, cog, R;  // channels per group, reduction length cig * K
   bool w_vec;       // W rows are 16-byte multiples and aligned: cp.async path
+  bool x_win;       // stride 1 and x 16-byte aligned: windowed 16-byte gather
   FastDivU32 div_k;
   int* err;
 };
 
 __device__ __forceinline__ uint32_t ig_swz(int r, int u) {
   return static_cast<uint32_t>(r * 128 + ((u ^ (r & 7)) << 4));
+}
+
+// Elements m..m+7 (16-bit) of the 16 elements in (a, b): the two 16-byte
+// loads that cover an unaligned 8-element window, funnel-shifted into place.
+__device__ __forceinline__ uint4 ig_window(const uint4& a, const uint4& b, int m) {
+  auto fs = [](uint32_t lo, uint32_t hi) { return __funnelshift_r(lo, hi, 16); };
+  switch (m) {
+    case 0: return a;
+    case 1: return make_uint4(fs(a.x, a.y), fs(a.y, a.z), fs(a.z, a.w), fs(a.w, b.x));
+    case 2: return make_uint4(a.y, a.z, a.w, b.x);
+    case 3: return make_uint4(fs(a.y, a.z), fs(a.z, a.w), fs(a.w, b.x), fs(b.x, b.y));
+    case 4: return make_uint4(a.z, a.w, b.x, b.y);
+    case 5: return make_uint4(fs(a.z, a.w), fs(a.w, b.x), fs(b.x, b.y), fs(b.y, b.z));
+    case 6: return make_uint4(a.w, b.x, b.y, b.z);
+    default: return make_uint4(fs(a.w, b.x), fs(b.x, b.y), fs(b.y, b.z), fs(b.z, b.w));
+  }
 }
 
 template <typename T>
@@ -370,11 +388,44 @@ __global__ void __launch_bounds__(kIgThreads) conv1d_igemm(const IgParams p) {
         }
       }
     }
-    // B: thread -> position o0 + (tid & 127), rows rr = tid >> 7, + 2, ...
-    // (the row table of this stage was written before the barrier that
-    // preceded this call)
+    // B = X[r0.., o0..]: MN-major, 64-position chunks 8 KB apart.  (The row
+    // table of this stage was written before the barrier preceding this call.)
     const int64_t* tb = rtab + (c & 1) * kIgK * 2;
     uint8_t* bt = st + kIgM * kIgK * 2;
+    if (p.x_win) {
+      // Row rr of the slice is the window x[ci, o0 - pad + k dil + (0..127)]:
+      // thread -> 16-byte units i = tid + 256 q (row i / 16, positions
+      // 8 (i % 16)..), each from two aligned 16-byte loads and a funnel shift;
+      // units that cross a row edge or the end of x go element by element.
+#pragma unroll
+      for (int q = 0; q < kIgK * kIgN / 8 / kIgThreads; ++q) {
+        const int i = tid + q * kIgThreads;
+        const int rr = i >> 4, u = i & 15;
+        const int64_t coff = tb[2 * rr];
+        const int64_t pos = static_cast<int64_t>(o0) - p.pad_left + tb[2 * rr + 1] + u * 8;
+        uint4 val = make_uint4(0u, 0u, 0u, 0u);
+        if (coff >= 0) {
+          const T* src = xg + coff + pos;
+          const uintptr_t a16 = reinterpret_cast<uintptr_t>(src) & ~static_cast<uintptr_t>(15);
+          const int m = static_cast<int>((reinterpret_cast<uintptr_t>(src) - a16) >> 1);
+          if (pos >= 0 && pos + 8 <= p.l_in &&
+              a16 + 32 <= reinterpret_cast<uintptr_t>(p.x_end)) {
+            const uint4 lo = *reinterpret_cast<const uint4*>(a16);
+            const uint4 hi = m ? *reinterpret_cast<const uint4*>(a16 + 16) : lo;
+            val = ig_window(lo, hi, m);
+          } else {
+            T* e = reinterpret_cast<T*>(&val);
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              e[j] = (pos + j >= 0 && pos + j < p.l_in) ? src[j] : Cvt<T>::from_f(0.0f);
+          }
+        }
+        // unit u of row rr: chunk u / 8 (8 KB apart), unit u % 8 of the 128-byte row
+        *reinterpret_cast<uint4*>(bt + (u >> 3) * (kIgK * 128) + ig_swz(rr, u & 7)) = val;
+      }
+      return;
+    }
+    // Any stride: thread -> position o0 + (tid & 127), rows rr = tid >> 7, + 2, ...
     const int oo = tid & (kIgN - 1);
     const int64_t pos0 = static_cast<int64_t>(o0 + oo) * p.stride - p.pad_left;
     const bool o_ok = o0 + oo < p.l_out;
@@ -515,6 +566,7 @@ int launch_igemm(const void* x, const void* w, const void* bias, void* y, int64_
                  int pad_left, int dil, int64_t groups, cudaStream_t s) {
   IgParams p;
   p.x = x;
+  p.x_end = static_cast<const T*>(x) + n * c_in * l_in;
   p.w = w;
   p.bias = bias;
   p.y = y;
@@ -531,6 +583,7 @@ int launch_igemm(const void* x, const void* w, const void* bias, void* y, int64_
   p.cog = static_cast<int>(c_out / groups);
   p.R = p.cig * K;
   p.w_vec = p.R % 8 == 0 && aligned16(w);
+  p.x_win = stride == 1 && aligned16(x);
   p.div_k = FastDivU32(static_cast<uint32_t>(K));
   p.err = device_error_ptr();
   auto k = conv1d_igemm<T>;
