@@ -379,6 +379,42 @@ def _ssd() -> Workload:
     )
 
 
+def _conv_dense() -> Workload:
+    from tileops.ops.convolution import Conv1dBiasFwdOp
+
+    N, CI, L, CO, K = 1, 80, 3000, 1280, 3
+
+    def make(dev, seed):
+        g = torch.Generator(device="cpu").manual_seed(seed)
+        x = torch.randn(N, CI, L, generator=g).to(torch.float16)
+        w = (torch.randn(CO, CI, K, generator=g) * 0.1).to(torch.float16)
+        b = (torch.randn(CO, generator=g) * 0.1).to(torch.float16)
+        return tuple(t.to(dev) for t in (x, w, b))
+
+    def cpu(inp):
+        from oracle import reference as ref
+
+        return ref.conv1d(inp[0], inp[1], inp[2], 1, 0, 1, 1)
+
+    def sample(inp, rows):  # a slice of the output channels
+        co = max(8, min(CO, rows))
+        return (inp[0], inp[1][:co], inp[2][:co])
+
+    def units(inp):
+        co = inp[1].shape[0]
+        return float(2 * N * co * CI * (L - K + 1) * K)
+
+    return Workload(
+        name="conv1d_dense", unit="TFLOP/s", dtype="f16", bound="tensor",
+        metric="achieved TFLOP/s (Conv1dBiasFwdOp, dense)",
+        config={"workload": "Conv1dBiasFwdOp x (1, 80, 3000) f16, weight (1280, 80, 3), bias, "
+                            "stride 1, no padding (manifest whisper-conv1-bias)"},
+        make_inputs=make, build_op=lambda: Conv1dBiasFwdOp(),
+        run=lambda op, inp: op(*inp), work_per_step=lambda op: float(op.eval_roofline()[0]),
+        kernel_regex="conv1d_igemm", cpu_fn=cpu, cpu_slice=sample, cpu_units=units,
+    )
+
+
 def workloads() -> dict[str, Callable[[], Workload]]:
     table = {
         "fused_add_layer_norm": _faln,
@@ -391,6 +427,7 @@ def workloads() -> dict[str, Callable[[], Workload]]:
         "gdn": _gdn,
         "gla_decode": _gla,
         "ssd_chunk_scan": _ssd,
+        "conv1d_dense": _conv_dense,
     }
     for kind in ("hardswish", "hardsigmoid", "clamp_scalar", "isnan", "isinf", "isfinite",
                  "bitwise_not"):
