@@ -133,3 +133,23 @@ def test_deterministic():
     outs = [op(*inputs) for _ in range(3)]
     for y, s in outs[1:]:
         assert torch.equal(y, outs[0][0]) and torch.equal(s, outs[0][1])
+
+
+@pytest.mark.parametrize("n", [1024, 1032, 2000, 3000, 4096])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("f32_affine", [False, True])
+def test_many_rows_per_width(n, dtype, f32_affine):
+    """Enough rows for the one-warp-per-row kernel: every packets-per-lane
+    instantiation (4, 8, 12, 16) and widths whose last lane packets are
+    partly empty; residual_out bit-exact, y at the reference tolerance."""
+    m = 700
+    x = torch.randn(m, n, dtype=dtype, device="cuda")
+    r = torch.randn(m, n, dtype=dtype, device="cuda")
+    wdt = torch.float32 if f32_affine else dtype
+    w = (1.0 + 0.1 * torch.randn(n, device="cuda")).to(wdt)
+    b = (0.1 * torch.randn(n, device="cuda")).to(wdt)
+    y, added = FusedAddLayerNormFwdOp(dtype=dtype)(x, r, w, b)
+    y_ref, added_ref = ref.fused_add_layer_norm(x, r, w, b)
+    atol, rtol = TOL[dtype]
+    torch.testing.assert_close(y.cpu(), y_ref, atol=atol, rtol=rtol)
+    assert torch.equal(added.cpu(), added_ref)
