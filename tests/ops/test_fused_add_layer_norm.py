@@ -139,9 +139,10 @@ def test_deterministic():
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("f32_affine", [False, True])
 def test_many_rows_per_width(n, dtype, f32_affine):
-    """Enough rows for the one-warp-per-row kernel: every packets-per-lane
-    instantiation (4, 8, 12, 16) and widths whose last lane packets are
-    partly empty; residual_out bit-exact, y at the reference tolerance."""
+    """Enough rows for the persistent ring kernel at widths of 1024..4096,
+    including widths whose last thread packets are partly empty; weight and
+    bias in the row dtype or fp32; residual_out bit-exact, y at the
+    reference tolerance."""
     m = 700
     x = torch.randn(m, n, dtype=dtype, device="cuda")
     r = torch.randn(m, n, dtype=dtype, device="cuda")
