@@ -139,11 +139,14 @@ int tileops_conv1d_depthwise_fwd(const void* x, const void* w, const void* bias,
                                  int64_t dilation, int dtype, int w_dtype, int activation,
                                  void* stream);
 
-/* General grouped conv1d (any groups, stride, dilation, padding), fp32
- * accumulation on CUDA cores: the dense/grouped conv1d kernels of the
- * reference (kernels/convolution/conv1d/conv1d.py:152-516: pointwise, generic,
- * unit-stride and group kernels).  x (n, c_in, l_in), w (c_out, c_in/groups, k),
- * bias (c_out,) or NULL, y (n, c_out, l_out). */
+/* General grouped conv1d (any groups, stride, dilation, padding) with fp32
+ * accumulation: the dense/grouped conv1d kernels of the reference
+ * (kernels/convolution/conv1d/conv1d.py:152-516: pointwise, generic,
+ * unit-stride and group kernels).  f16 / bf16 run as an implicit GEMM on
+ * tcgen05 tensor cores (bias added in fp32, one rounding); f32 on CUDA cores.
+ * x (n, c_in, l_in), w (c_out, c_in/groups, k) and bias (c_out,) or NULL in
+ * `dtype`, y (n, c_out, l_out).  A bounded device-side wait that times out is
+ * reported through tileops_device_error_flag. */
 int tileops_conv1d_direct_fwd(const void* x, const void* w, const void* bias, void* y,
                               int64_t n, int64_t c_in, int64_t l_in, int64_t c_out,
                               int64_t l_out, int64_t k, int64_t stride, int64_t pad_left,
