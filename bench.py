@@ -415,6 +415,59 @@ def _conv_dense() -> Workload:
     )
 
 
+def _gdn_varlen() -> Workload:
+    import torch.nn.functional as F
+
+    from tileops.ops.linear_attention import GatedDeltaNetPrefillFwdOp
+
+    TOTAL, H, DK, DV = 4 * 8192, 16, 128, 128
+    # 12 sequences of ragged lengths (seeded), 32768 tokens in all: the
+    # BASELINE token count packed fla-style (batch 1, cu_seqlens).
+    gl = torch.Generator(device="cpu").manual_seed(7)
+    cuts = sorted(torch.randint(1, TOTAL, (11,), generator=gl).tolist())
+    offsets = [0] + cuts + [TOTAL]
+
+    def make(dev, seed):
+        g_ = torch.Generator(device="cpu").manual_seed(seed)
+        q = F.normalize(torch.randn(1, TOTAL, H, DK, generator=g_), dim=-1).to(torch.bfloat16)
+        k = F.normalize(torch.randn(1, TOTAL, H, DK, generator=g_), dim=-1).to(torch.bfloat16)
+        v = torch.randn(1, TOTAL, H, DV, generator=g_).to(torch.bfloat16)
+        g = F.logsigmoid(torch.randn(1, TOTAL, H, generator=g_)) / 16
+        beta = torch.sigmoid(torch.randn(1, TOTAL, H, generator=g_))
+        cu = torch.tensor(offsets, dtype=torch.int32)
+        return tuple(t.to(dev) for t in (q, k, v, g, beta, cu))
+
+    def cpu(inp):
+        from oracle import reference as ref
+
+        return ref.gdn_prefill_varlen(*inp[:5], inp[5])
+
+    def sample(inp, rows):  # the first sequence's first tokens, one head
+        t = max(64, min(offsets[1], rows * 4))
+        return tuple(x[:1, :t, :1].contiguous() for x in inp[:5]) + (
+            torch.tensor([0, t], dtype=torch.int32),)
+
+    def units(inp):
+        t = inp[0].shape[1]
+        return float(t * (4 * 64 * DK + 6 * DK * DV + 3 * 64 * DV))
+
+    return Workload(
+        name="gdn_varlen", unit="TFLOP/s", dtype="bf16", bound="hbm", roof_unit="GB/s",
+        roof_work_per_step=lambda op: float(op.eval_roofline()[1]),
+        metric="achieved TFLOP/s (GatedDeltaNetPrefillFwdOp, packed cu_seqlens)",
+        config={"workload": "GatedDeltaNetPrefillFwdOp packed: 32768 tokens (the BASELINE "
+                            "token count) in 12 seeded ragged sequences, H=16 dk=dv=128, "
+                            "chunk 64, same input distributions as the BASELINE config",
+                "cu_seqlens": offsets},
+        make_inputs=make,
+        build_op=lambda: GatedDeltaNetPrefillFwdOp(1, TOTAL, H, DK, DV),
+        run=lambda op, inp: op(*inp[:5], None, cu_seqlens=inp[5]),
+        work_per_step=lambda op: float(op.eval_roofline()[0]),
+        kernel_regex="gdn_", cpu_fn=cpu, cpu_slice=sample, cpu_units=units,
+        launches_per_step=3,  # chunk index + prepare + scan
+    )
+
+
 def workloads() -> dict[str, Callable[[], Workload]]:
     table = {
         "fused_add_layer_norm": _faln,
@@ -425,6 +478,7 @@ def workloads() -> dict[str, Callable[[], Workload]]:
         "mha": lambda: _mha(False),
         "mha_causal": lambda: _mha(True),
         "gdn": _gdn,
+        "gdn_varlen": _gdn_varlen,
         "gla_decode": _gla,
         "ssd_chunk_scan": _ssd,
         "conv1d_dense": _conv_dense,
