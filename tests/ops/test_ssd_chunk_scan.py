@@ -126,3 +126,13 @@ def test_contract_and_validation():
         op(x.cpu(), cb, dA, Cm, prev, dt)
     with pytest.raises(ValueError, match="cb.dtype"):
         op(x, cb.bfloat16(), dA, Cm, prev, dt)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("Q, P, N, G, dtype", [
+    (100, 16, 8, 1, torch.bfloat16),    # chunk not a multiple of 8: element cb loads
+    (72, 32, 24, 2, torch.float16),
+    (130, 128, 256, 1, torch.bfloat16),  # largest head and state, a 2-row second tile
+])
+def test_small_and_ragged_dims(Q, P, N, G, dtype):
+    _case(2, 3, Q, 4, P, N, G, dtype, seed=50 + Q)
