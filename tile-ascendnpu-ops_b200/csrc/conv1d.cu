@@ -286,6 +286,7 @@ struct IgParams {
   int cig, cog, R;  // channels per group, reduction length cig * K
   bool w_vec;       // W rows are 16-byte multiples and aligned: cp.async path
   bool x_win;       // stride 1 and x 16-byte aligned: windowed 16-byte gather
+  bool y_pair;      // rows of y start 4-byte aligned: paired stores in the epilogue
   FastDivU32 div_k;
   int* err;
 };
@@ -544,11 +545,30 @@ __global__ void __launch_bounds__(kIgThreads) conv1d_igemm(const IgParams p) {
     const int nrow = min(kIgM, p.cog - co0), ncol = min(kIgN, static_cast<int>(p.l_out - o0));
     T* ybase = static_cast<T*>(p.y) +
                (b * p.c_out + static_cast<int64_t>(g) * p.cog + co0) * p.l_out + o0;
+    // Element pairs as 4-byte stores when every row starts 4-byte aligned
+    // (y aligned, l_out and o0 even): lane l writes columns 2l, 2l + 1,
+    // 2l + 64, 2l + 65 of its warp's rows; otherwise single elements.
+    const bool pairs = p.y_pair && (ncol & 1) == 0;
     for (int rr = warp; rr < nrow; rr += kIgThreads / 32) {
       T* yr = ybase + static_cast<int64_t>(rr) * p.l_out;
-      for (int c = tid & 31; c < ncol; c += 32) {
-        const int u = c >> 3;
-        yr[c] = *reinterpret_cast<const T*>(stg + rr * 256 + ((u ^ (rr & 15)) << 4) + (c & 7) * 2);
+      const uint8_t* sr = stg + rr * 256;
+      if (pairs) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int c = 2 * (tid & 31) + 64 * h;
+          if (c < ncol) {
+            const uint32_t v =
+                *reinterpret_cast<const uint32_t*>(sr + (((c >> 3) ^ (rr & 15)) << 4) + (c & 7) * 2);
+            *reinterpret_cast<uint32_t*>(yr + c) = v;
+          }
+        }
+      } else {
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const int c = (tid & 31) + 32 * h;
+          if (c < ncol)
+            yr[c] = *reinterpret_cast<const T*>(sr + (((c >> 3) ^ (rr & 15)) << 4) + (c & 7) * 2);
+        }
       }
     }
   }
@@ -584,6 +604,7 @@ int launch_igemm(const void* x, const void* w, const void* bias, void* y, int64_
   p.R = p.cig * K;
   p.w_vec = p.R % 8 == 0 && aligned16(w);
   p.x_win = stride == 1 && aligned16(x);
+  p.y_pair = (reinterpret_cast<uintptr_t>(y) & 3u) == 0 && l_out % 2 == 0;
   p.div_k = FastDivU32(static_cast<uint32_t>(K));
   p.err = device_error_ptr();
   auto k = conv1d_igemm<T>;
