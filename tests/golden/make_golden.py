@@ -102,7 +102,8 @@ def corner_values(dtype: torch.dtype) -> torch.Tensor:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference", type=Path)
+    ap.add_argument("--reference", required=True, type=Path,
+                    help="checkout of the reference repository")
     ap.add_argument("--only", nargs="*", default=[],
                     help="write only fixtures whose name starts with one of these")
     args = ap.parse_args()

@@ -59,6 +59,7 @@ constexpr int kSoftmaxThreads = 128 * kTiles;
 constexpr int kThreads = kSoftmaxThreads + 64;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
+constexpr int kGroupBH = 16;  // (b, h) pairs per launch-order group
 
 template <int D>
 struct Smem {
@@ -122,8 +123,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int num_ct = (p.seq_q + kTiles * kBM - 1) / (kTiles * kBM);
-  const int ct = num_ct - 1 - static_cast<int>(blockIdx.x);  // longest causal tiles first
-  const int bh = blockIdx.y;
+  // CTAs start in linear grid order.  That order walks groups of kGroupBH
+  // (b, h) pairs; inside a group the longest (causal) query tiles of all its
+  // pairs come first, so the grid ends on short CTAs while the K / V of the
+  // few pairs in flight stay in L2.
+  const int nbh = static_cast<int>(gridDim.y);
+  const int lin = static_cast<int>(blockIdx.y) * num_ct + static_cast<int>(blockIdx.x);
+  const int grp = lin / (kGroupBH * num_ct);
+  const int gsz = min(kGroupBH, nbh - grp * kGroupBH);
+  const int within = lin - grp * kGroupBH * num_ct;
+  const int ct = num_ct - 1 - within / gsz;
+  const int bh = grp * kGroupBH + within % gsz;
   const int b = bh / p.heads;
   const int h = bh - b * p.heads;
   const int hk = h / (p.heads / p.heads_kv);
@@ -451,6 +461,9 @@ extern "C" int tileops_mha_fwd(const void* q, const void* k, const void* v, void
   if (dim != 64 && dim != 128) return TILEOPS_EBADSHAPE;
   if (is_causal && seq_q > seq_kv) return TILEOPS_EBADSHAPE;
   if (batch * heads > 65535 || seq_q > (1 << 30) || seq_kv > (1 << 30)) return TILEOPS_EBADSHAPE;
+  // The kernel numbers its CTAs with a 32-bit linear index.
+  if ((seq_q + kTiles * kBM - 1) / (kTiles * kBM) * batch * heads > 0x7fffffffLL)
+    return TILEOPS_EBADSHAPE;
   if (dtype != TILEOPS_DT_BF16 && dtype != TILEOPS_DT_F16) return TILEOPS_EBADDTYPE;
   if (batch == 0 || seq_q == 0) return TILEOPS_OK;
   if (seq_kv == 0) return TILEOPS_EBADSHAPE;  // no key to attend to
