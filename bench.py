@@ -616,6 +616,51 @@ def barrier(world: int, device) -> None:
             dist.barrier()
 
 
+def gather_outputs(outs, world: int, device, reps: int = 5):
+    """Reassemble every rank's output shards on every rank: one
+    ``all_gather_into_tensor`` per output tensor (NCCL over NVLink on GPUs,
+    gloo on CPU ranks).  It moves results only -- no op needs data from
+    another rank -- so it is timed apart from the op: the mean of ``reps``
+    rounds, the max over ranks.  Returns (summary, gathered tensors)."""
+    import torch.distributed as dist
+
+    flats = [o.contiguous().view(-1) for o in outs]
+    fulls = [torch.empty(world * f.numel(), dtype=f.dtype, device=f.device) for f in flats]
+
+    def one_round():
+        for full, flat in zip(fulls, flats):
+            dist.all_gather_into_tensor(full, flat)
+
+    one_round()  # warm-up; its result is what the caller checks
+    barrier(world, device)
+    if device.type == "cuda":
+        torch.cuda.synchronize(device)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(torch.cuda.current_stream(device))
+        for _ in range(reps):
+            one_round()
+        e1.record(torch.cuda.current_stream(device))
+        torch.cuda.synchronize(device)
+        ms = e0.elapsed_time(e1) / reps
+    else:
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            one_round()
+        ms = (time.perf_counter() - t0) * 1e3 / reps
+    ms = max_over_ranks(ms, world, device)
+    per_rank = sum(f.numel() * f.element_size() for f in flats)
+    total = world * per_rank
+    summary = {
+        "collective": "all_gather_into_tensor (output reassembly only)",
+        "outputs": len(flats), "bytes_per_rank": per_rank, "bytes_total": total,
+        "bytes_received_per_rank": (world - 1) * per_rank, "ms": ms,
+        "algbw_GBps": total / (ms * 1e-3) / 1e9,
+        "busbw_GBps": (world - 1) / world * total / (ms * 1e-3) / 1e9,
+    }
+    return summary, fulls
+
+
 def whole_job_value(work_per_step: float, steps: int, total_ms: float, world: int,
                     unit: str) -> float:
     """Weak scaling: every rank ran ``steps`` steps of ``work_per_step`` units;
@@ -760,6 +805,15 @@ def run_ours(args, wl: Workload) -> Optional[dict]:
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps, world, device)
     barrier(world, device)
 
+    gather = None
+    if args.gather and world > 1:
+        res = wl.run(op, sets[0])
+        res = res if isinstance(res, (tuple, list)) else (res,)
+        gather, fulls = gather_outputs(res, world, device)
+        gather["op_plus_gather_ms"] = per_launch_ms + gather["ms"]
+        del res, fulls
+        barrier(world, device)
+
     scale = 1e9 if wl.unit == "GB/s" else 1e12
     value = whole_job_value(work, args.steps, total_ms, world, wl.unit)
     roof_unit = wl.roof_unit or wl.unit
@@ -802,6 +856,8 @@ def run_ours(args, wl: Workload) -> Optional[dict]:
         "gpu_launches": args.steps * wl.launches_per_step,
         "clocks": clocks,
     }
+    if gather is not None:
+        line["gather"] = gather
     if world == 1 and not args.no_cpu_baseline and wl.cpu_fn is not None:
         line["cpu_baseline"] = time_cpu_baseline(wl)
     return line
@@ -854,6 +910,9 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", dest="graph", action="store_false",
                     help="time eager op calls instead of CUDA-graph replays")
+    ap.add_argument("--gather", action="store_true",
+                    help="N > 1: also time reassembling every rank's outputs on every rank "
+                         "(all_gather_into_tensor; reported under 'gather', not in 'value')")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

@@ -1,8 +1,9 @@
 """One rank of the multi-rank bench-path test (run under torchrun, gloo).
 
 Exercises, on CPU ranks, the host logic ``bench.py`` uses at N > 1: the
-barrier, the max-over-ranks reduction of the timed region, and the
-weak-scaling whole-job value.  Exits non-zero on a mismatch.
+barrier, the max-over-ranks reduction of the timed region, the
+weak-scaling whole-job value and the optional output reassembly
+(``gather_outputs``).  Exits non-zero on a mismatch.
 """
 
 import datetime
@@ -31,6 +32,18 @@ def main() -> int:
     ok = got == expect
     value = bench.whole_job_value(1e9, 4, got, world, "GB/s")
     ok &= abs(value - world * 4.0 / (expect * 1e-3)) < 1e-9
+    # Output reassembly (bench.py --gather): every rank ends up with every
+    # rank's shards, in rank order, and the byte counts follow the shapes.
+    outs = (torch.full((3, 4), float(rank)), torch.arange(5, dtype=torch.int32) + 10 * rank)
+    summary, fulls = bench.gather_outputs(outs, world, dev, reps=2)
+    for r in range(world):
+        ok &= bool(torch.equal(fulls[0][12 * r:12 * (r + 1)], torch.full((12,), float(r))))
+        ok &= bool(torch.equal(fulls[1][5 * r:5 * (r + 1)],
+                               torch.arange(5, dtype=torch.int32) + 10 * r))
+    ok &= summary["bytes_per_rank"] == 12 * 4 + 5 * 4
+    ok &= summary["bytes_total"] == world * (12 * 4 + 5 * 4)
+    ok &= summary["bytes_received_per_rank"] == (world - 1) * (12 * 4 + 5 * 4)
+    ok &= summary["outputs"] == 2 and summary["ms"] > 0
     bench.barrier(world, dev)
     dist.destroy_process_group()
     print(f"rank {rank}/{world} local {local_rank} max {got} value {value:.6f} "
