@@ -143,3 +143,10 @@ def test_mha_validation():
     assert lib.tileops_mha_fwd(*args, 1, 4, 4, 64, 64, 128, 0, 0.1, 0, NULL) == _native.EBADDTYPE
     assert lib.tileops_mha_fwd(*args, 1, 4, 4, 128, 64, 128, 1, 0.1, 2, NULL) == (
         _native.EBADSHAPE)
+    # More CTAs than a 32-bit linear block index can number (64 x 1023 heads
+    # x 2^22 query-tile pairs) is refused, not launched.
+    assert lib.tileops_mha_fwd(*args, 64, 1023, 1023, 1 << 30, 1 << 30, 128, 0, 0.1, 2,
+                               NULL) == _native.EBADSHAPE
+    # Batch x heads above the grid's y limit.
+    assert lib.tileops_mha_fwd(*args, 2, 32768, 32768, 64, 64, 128, 0, 0.1, 2, NULL) == (
+        _native.EBADSHAPE)
