@@ -16,7 +16,9 @@ ref programs / goldens (from the reference checkout, in the build container)
 on seeded inputs and commits the results as fixtures; ``tests/test_oracle.py``
 checks every function here against those fixtures.  GDN prefill has no
 reference test; its oracle is pinned to the reference's sequential golden
-(examples/gdn_prefill/probe/gdn_prefill_probe.py:60-77) only.
+(examples/gdn_prefill/probe/gdn_prefill_probe.py:60-77) and cross-checked
+against flash-linear-attention's CPU reference recurrence (the probe's
+ref_api library).
 """
 
 from oracle import reference

@@ -160,3 +160,32 @@ def test_oracle_ssd_chunk_scan(name):
     out = ref.ssd_chunk_scan(i["x"], i["cb"], i["dA_cumsum"], i["C"], i["prev_states"], i["dt"],
                              m["n_groups"])
     torch.testing.assert_close(out, case["outputs"]["out"], atol=1e-6, rtol=1e-5)
+
+
+def test_oracle_gdn_matches_fla_naive_recurrence():
+    """Second, independent pin of the GDN oracle: flash-linear-attention's own
+    CPU reference (``fla.ops.gated_delta_rule.naive.naive_recurrent_gated_delta_rule``,
+    fla 0.5.1 -- the ref_api the reference's GDN probe names) on the same fp32
+    inputs, with an initial state and a ragged length, batch and packed forms."""
+    naive = pytest.importorskip("fla.ops.gated_delta_rule.naive")
+    torch.manual_seed(11)
+    b, t, h, dk, dv = 2, 37, 3, 16, 8
+    q = torch.nn.functional.normalize(torch.randn(b, t, h, dk), dim=-1)
+    k = torch.nn.functional.normalize(torch.randn(b, t, h, dk), dim=-1)
+    v = torch.randn(b, t, h, dv)
+    g = torch.nn.functional.logsigmoid(torch.randn(b, t, h)) / 16
+    beta = torch.sigmoid(torch.randn(b, t, h))
+    h0 = torch.randn(b, h, dk, dv) * 0.1
+    o, s = ref.gdn_prefill_bthd(q, k, v, g, beta, 0.3, h0)
+    o_f, s_f = naive.naive_recurrent_gated_delta_rule(q, k, v, beta, g, scale=0.3,
+                                                      initial_state=h0,
+                                                      output_final_state=True)
+    torch.testing.assert_close(o, o_f, atol=1e-5, rtol=1e-5)
+    torch.testing.assert_close(s, s_f, atol=1e-5, rtol=1e-5)
+    # Packed: two sequences along the token axis, each from its own state.
+    flat = lambda x: x.reshape(1, b * t, *x.shape[2:])  # noqa: E731
+    cu = torch.tensor([0, t, 2 * t], dtype=torch.int32)
+    o_p, s_p = ref.gdn_prefill_varlen(flat(q), flat(k), flat(v), flat(g), flat(beta), cu,
+                                      0.3, h0)
+    torch.testing.assert_close(o_p, flat(o_f), atol=1e-5, rtol=1e-5)
+    torch.testing.assert_close(s_p, s_f, atol=1e-5, rtol=1e-5)
