@@ -189,3 +189,66 @@ def test_oracle_gdn_matches_fla_naive_recurrence():
                                       0.3, h0)
     torch.testing.assert_close(o_p, flat(o_f), atol=1e-5, rtol=1e-5)
     torch.testing.assert_close(s_p, s_f, atol=1e-5, rtol=1e-5)
+
+
+def test_oracle_gla_decode_matches_fla_naive_recurrence():
+    """The GLA decode oracle applied token by token equals
+    flash-linear-attention's CPU reference recurrence
+    (``fla.ops.gla.naive.naive_recurrent_gla``) over the same tokens: every
+    step's output and the final state (fp32, fla's default scale K^-0.5)."""
+    naive = pytest.importorskip("fla.ops.gla.naive")
+    torch.manual_seed(12)
+    b, t, h, dk, dv = 2, 9, 3, 16, 8
+    q, k = torch.randn(b, t, h, dk), torch.randn(b, t, h, dk)
+    v = torch.randn(b, t, h, dv)
+    gk = torch.nn.functional.logsigmoid(torch.randn(b, t, h, dk))
+    h0 = torch.randn(b, h, dk, dv)
+    o_f, s_f = naive.naive_recurrent_gla(q, k, v, gk, initial_state=h0,
+                                         output_final_state=True)
+    state = h0
+    for i in range(t):
+        o_i, state = ref.gla_decode(q[:, i], k[:, i], v[:, i], gk[:, i], state, dk ** -0.5)
+        torch.testing.assert_close(o_i, o_f[:, i], atol=1e-5, rtol=1e-5)
+    torch.testing.assert_close(state, s_f, atol=1e-5, rtol=1e-5)
+
+
+def test_oracle_ssd_chunk_scan_matches_the_token_recurrence():
+    """The SSD chunk-scan oracle from first principles (Mamba-2's state-space
+    recurrence, per head h in group g = h // (H / G)):
+
+        state_t = exp(dt_t A_h) state_{t-1} + dt_t x_t B_t^T     (P x N)
+        y_t     = state_t C_t
+
+    run token by token in fp64.  The chunk scan's inputs are derived from it:
+    cb[l, s] = C_l . B_s, dA_cumsum = the inclusive in-chunk cumsum of dt A,
+    prev_states[c] = the state entering chunk c.  Its output must equal y."""
+    torch.manual_seed(13)
+    b, nc, L, h, p, n, g = 2, 3, 8, 4, 4, 6, 2
+    seq = nc * L
+    x = torch.randn(b, seq, h, p, dtype=torch.float64)
+    Bm = torch.randn(b, seq, g, n, dtype=torch.float64)
+    Cm = torch.randn(b, seq, g, n, dtype=torch.float64)
+    dt = torch.nn.functional.softplus(torch.randn(b, seq, h, dtype=torch.float64))
+    A = -torch.rand(h, dtype=torch.float64) - 0.1
+    grp = torch.arange(h) // (h // g)
+
+    state = torch.zeros(b, h, p, n, dtype=torch.float64)
+    y = torch.zeros(b, seq, h, p, dtype=torch.float64)
+    prev = torch.zeros(b, nc, h, p, n, dtype=torch.float64)
+    for t in range(seq):
+        if t % L == 0:
+            prev[:, t // L] = state
+        decay = torch.exp(dt[:, t] * A)                                   # b h
+        Bt, Ct = Bm[:, t][:, grp], Cm[:, t][:, grp]                       # b h n
+        state = state * decay[..., None, None] + \
+            (dt[:, t][..., None] * x[:, t])[..., None] * Bt[:, :, None, :]
+        y[:, t] = torch.einsum("bhpn,bhn->bhp", state, Ct)
+
+    Bc = Bm.reshape(b, nc, L, g, n)
+    Cc = Cm.reshape(b, nc, L, g, n)
+    cb = torch.einsum("bclgn,bcsgn->bcgls", Cc, Bc)                         # B NC G L L
+    dA = torch.cumsum((dt * A).reshape(b, nc, L, h), dim=2).permute(0, 3, 1, 2)  # B H NC L
+    dt_c = dt.reshape(b, nc, L, h).permute(0, 3, 1, 2)                      # B H NC L
+    out = ref.ssd_chunk_scan(x.float(), cb.float(), dA.float(), Cm.float(), prev.float(),
+                             dt_c.float(), g)
+    torch.testing.assert_close(out.double(), y, atol=1e-4, rtol=1e-4)
