@@ -58,3 +58,20 @@ def test_gdn_varlen_argument_checks_without_gpu():
     g = torch.zeros(1, 64, 1)
     with pytest.raises(ValueError, match="must be a"):
         op(q, q, q, g, g, cu_seqlens=torch.tensor([0, 64], dtype=torch.int32))
+
+
+def test_gla_manifest_rows_and_roofline():
+    """Every GLADecodeOp manifest row builds an op whose eval_roofline is the
+    manifest formula (reference linear_attention.yaml GLADecodeOp roofline)."""
+    from tileops.manifest import load_manifest, load_workloads
+
+    assert "SSDChunkScanFwdOp" in load_manifest()
+    rows = load_workloads("GLADecodeOp")
+    assert rows
+    for row in rows:
+        for dt in row["dtypes"]:
+            dtype = getattr(torch, dt)
+            b, h, dk, dv = row["B"], row["H"], row["DK"], row["DV"]
+            flops, nbytes = GLADecodeOp(b, h, dk, dv, row["scale"], dtype).eval_roofline()
+            assert flops == b * h * (5 * dk * dv + dk + dv)
+            assert nbytes == b * h * (3 * dk + 2 * dv + 2 * dk * dv) * dtype.itemsize
