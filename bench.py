@@ -1,27 +1,39 @@
 """Benchmark of the hot path on B200: one JSON line per run.
 
-Default workload: FusedAddLayerNormFwdOp on x, residual
+Headline: FusedAddLayerNormFwdOp on x, residual
 (8192, 4096) bf16 ~ N(0, 1) with fp32 weight = 1 + 0.1 N(0,1), bias =
-0.1 N(0,1), eps 1e-5.  A step is one forward over that batch.  ``--op``
-selects another hot-path op at its BASELINE configuration (used for the
-per-op tables; the default line is the contract's headline).
+0.1 N(0,1), eps 1e-5.  ``--op`` picks another headline op.  The same line
+carries ``per_op``: every other hot-path op at its BASELINE configuration
+(plus, at N = 1, the reference-manifest workloads of the ops beyond
+BASELINE), each timed with the same protocol and with its own roofline,
+end-to-end figure, clock record and CPU baseline.
 
-Metric: achieved HBM GB/s = algorithmic bytes of the op (its eval_roofline
-bytes) / time, summed over ranks (weak scaling: every rank runs its own
-batch, no collective on the data path).  MHA / GDN lines report TFLOP/s.
+One GPU (N = 1): a step is one op call over the whole BASELINE problem.
+The K timed steps replay a CUDA graph of up to 64 consecutive calls, each
+with its own outputs, inputs rotating over buffer sets whose total exceeds
+the 126 MB L2 (so no step finds its inputs in L2); CUDA events around every
+replay.  ``value`` = algorithmic work (the op's ``eval_roofline``) x K /
+that time.
 
-Timing: W warm-up steps, then K steps bracketed by a barrier and
-``torch.cuda.synchronize()``, CUDA events on the launching stream around
-every graph replay, max over ranks.  The K steps run as replays of a CUDA
-graph holding up to 64 consecutive op calls, each with its own outputs
-(``--no-graph``: K eager calls, which the host's Python cost can starve when
-a kernel is ~50 us).  Inputs rotate over enough distinct buffer sets
-that every step's working set was evicted from the 126 MB L2 (the set count
-is in ``config``).  ``e2e`` repeats the measurement through the public op API
-with pinned HOST buffers: H2D of the inputs, the op, D2H of the outputs.
+N GPUs (torchrun, one rank per GPU, NCCL): the SAME BASELINE problem is
+split across the ranks (rows / batches / (batch, head) pairs; every rank
+draws the full problem from the same seed and keeps its slice), and a step
+is the op on the rank's shard followed by the reassembly of every output on
+every rank (``all_gather_into_tensor`` over NVLink; a local permute when
+heads were split).  ``value`` = the problem's work x K / the slowest rank's
+time for K such steps: strong scaling.  ``kernel_only`` gives the same
+problem timed without the reassembly, ``gather`` its bytes and time,
+``weak`` the old per-rank replica figure.
 
-``--impl reference`` times the reference's CPU path (the torch ref program,
-restated in ``oracle/``) on the host cores, rank 0 only.
+``e2e`` times the public op API from pinned HOST buffers: the problem (or
+the rank's shard) is cut into chunks; per chunk, the host-to-device copy,
+the op call and the device-to-host copy of its outputs run on three
+streams, so copies in both directions overlap the kernels.  ``cpu_baseline``
+(rank 0, N = 1) times the reference's own torch CPU program (restated in
+``oracle/``) on the full configuration wherever one call fits the time
+budget, with all host threads.
+
+``--impl reference`` times that CPU program instead (rank 0 only).
 
 Run: python bench.py [--gpus N] [--steps K] [--warmup W] [--op NAME] [--impl ours|reference]
 (N > 1: python -m torch.distributed.run --nproc-per-node N bench.py --gpus N ...)
@@ -48,6 +60,55 @@ import torch  # noqa: E402
 
 L2_BYTES = 126 * 1024 * 1024
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+SEED = 1235
+
+
+# ----------------------------------------------------------------- sharding
+def split_range(n: int, index: int, count: int) -> Optional[slice]:
+    """The index-th of ``count`` equal contiguous parts of range(n), or None
+    when n does not split evenly (``all_gather_into_tensor`` needs equal
+    shards on every rank)."""
+    if count < 1 or not 0 <= index < count or n % count:
+        return None
+    per = n // count
+    return slice(index * per, (index + 1) * per)
+
+
+def shard_axis0(t: torch.Tensor, index: int, count: int) -> Optional[torch.Tensor]:
+    s = split_range(t.shape[0], index, count)
+    return None if s is None else t[s].contiguous()
+
+
+def bh_split(batch: int, heads: int, index: int, count: int):
+    """(batch slice, head slice) of the index-th of ``count`` equal groups of
+    (batch, head) pairs, batch-major: whole batches while ``count`` divides
+    the batch, else equal head groups inside each batch."""
+    bs = split_range(batch, index, count)
+    if bs is not None:
+        return bs, slice(0, heads)
+    if count % batch:
+        return None
+    per_b = count // batch
+    hs = split_range(heads, index % per_b, per_b)
+    if hs is None:
+        return None
+    b = index // per_b
+    return slice(b, b + 1), hs
+
+
+def head_groups(batch: int, count: int) -> int:
+    """Head groups per batch in ``bh_split`` (1 when whole batches are split)."""
+    return 1 if batch % count == 0 else count // batch
+
+
+def unshard_bthd(flat: torch.Tensor, batch: int, seq: int, heads: int, dim: int,
+                 count: int) -> torch.Tensor:
+    """BTHD tensor from ``count`` gathered ``bh_split`` shards (rank-major)."""
+    g = head_groups(batch, count)
+    if g == 1:
+        return flat.view(batch, seq, heads, dim)
+    return (flat.view(batch, g, seq, heads // g, dim).permute(0, 2, 1, 3, 4)
+            .reshape(batch, seq, heads, dim))
 
 
 # ----------------------------------------------------------------- workloads
@@ -60,21 +121,51 @@ class Workload:
     unit: str  # "GB/s" or "TFLOP/s"
     dtype: str
     config: dict
-    make_inputs: Callable[[torch.device, int], tuple]  # (device, seed) -> device tensors
-    build_op: Callable[[], object]
+    make_inputs: Callable[[torch.device, int], tuple]  # the full problem on a device
+    build_op: Callable[[tuple], object]  # an op sized for these inputs
     run: Callable[[object, tuple], object]
-    work_per_step: Callable[[object], float]  # bytes (GB/s) or flops (TFLOP/s) per step
+    work: Callable[[object], float]  # bytes (GB/s) or flops (TFLOP/s) of one call of op
     kernel_regex: str
-    cpu_fn: Optional[Callable[[tuple], object]] = None  # oracle on CPU tensors
-    cpu_slice: Optional[Callable[[tuple, int], tuple]] = None  # bounded sample of the inputs
-    cpu_units: Optional[Callable[[tuple], float]] = None  # work units of a sample
+    cpu_ref: Optional[Callable[[tuple], object]] = None  # the reference's CPU program
+    cpu_sample: Optional[Callable[[tuple], tuple]] = None  # bounded part of the problem
+    cpu_sample_desc: str = ""
+    shard: Optional[Callable[[tuple, int, int], Optional[tuple]]] = None
+    shard_desc: str = ""
+    unshard: Optional[Callable[[list, int], list]] = None  # gathered flats -> full layout
     bound: str = "hbm"
     # Roofline of the dominant kernel when it is not in the metric's unit
-    # (GDN: metric TFLOP/s, bound HBM): work per step in that unit.
+    # (GDN: metric TFLOP/s, bound HBM): work per call in that unit.
     roof_unit: Optional[str] = None
-    roof_work_per_step: Optional[Callable[[object], float]] = None
-    launches_per_step: int = 1  # kernels of this library one step launches
+    roof_work: Optional[Callable[[object], float]] = None
+    launches_per_call: int = 1  # kernels of this library one call launches
+    baseline: bool = True  # one of BASELINE.json's configs
+    # ``work`` computed from input shapes alone, for ops whose eval_roofline
+    # binds the shape in forward (the CPU legs never call our kernels).
+    units: Optional[Callable[[tuple], float]] = None
     extra: dict = field(default_factory=dict)
+
+
+def host_work(wl: Workload, inputs: tuple) -> float:
+    """The op's algorithmic work for these inputs without launching it."""
+    if wl.units is not None:
+        return float(wl.units(inputs))
+    return float(wl.work(wl.build_op(inputs)))
+
+
+def _gen(dev, seed):
+    return torch.Generator(device=dev).manual_seed(seed)
+
+
+def _rows_shard(n_split: int):
+    """Shard the first ``n_split`` inputs along axis 0, keep the rest whole."""
+
+    def shard(inp, index, count):
+        parts = [shard_axis0(t, index, count) for t in inp[:n_split]]
+        if any(p is None for p in parts):
+            return None
+        return tuple(parts) + tuple(inp[n_split:])
+
+    return shard
 
 
 def _faln() -> Workload:
@@ -83,16 +174,12 @@ def _faln() -> Workload:
     M, N = 8192, 4096
 
     def make(dev, seed):
-        g = torch.Generator(device="cpu").manual_seed(seed)
-        x = torch.randn(M, N, generator=g).to(torch.bfloat16)
-        r = torch.randn(M, N, generator=g).to(torch.bfloat16)
-        w = 1.0 + 0.1 * torch.randn(N, generator=g)
-        b = 0.1 * torch.randn(N, generator=g)
-        return tuple(t.to(dev) for t in (x, r, w, b))
-
-    def units(inp):
-        m, n = inp[0].shape
-        return 4.0 * m * n * 2 + 2 * n * 4
+        g = _gen(dev, seed)
+        x = torch.randn(M, N, generator=g, device=dev).to(torch.bfloat16)
+        r = torch.randn(M, N, generator=g, device=dev).to(torch.bfloat16)
+        w = 1.0 + 0.1 * torch.randn(N, generator=g, device=dev)
+        b = 0.1 * torch.randn(N, generator=g, device=dev)
+        return x, r, w, b
 
     def cpu(inp):
         from oracle import reference as ref
@@ -105,11 +192,11 @@ def _faln() -> Workload:
         config={"workload": "FusedAddLayerNormFwdOp x,residual (8192,4096) bf16 + fp32 "
                             "weight/bias (N=4096), eps 1e-5 (BASELINE configs[1])",
                 "M": M, "N": N},
-        make_inputs=make, build_op=lambda: FusedAddLayerNormFwdOp(dtype=torch.bfloat16),
-        run=lambda op, inp: op(*inp), work_per_step=lambda op: float(op.eval_roofline()[1]),
-        kernel_regex="faln_", cpu_fn=cpu,
-        cpu_slice=lambda inp, rows: (inp[0][:rows], inp[1][:rows], inp[2], inp[3]),
-        cpu_units=units,
+        make_inputs=make, build_op=lambda inp: FusedAddLayerNormFwdOp(dtype=torch.bfloat16),
+        run=lambda op, inp: op(*inp), work=lambda op: float(op.eval_roofline()[1]),
+        kernel_regex="faln_", cpu_ref=cpu, shard=_rows_shard(2), shard_desc="rows of M",
+        units=lambda inp: (4 * inp[0].numel() * inp[0].element_size()
+                           + 2 * inp[2].numel() * inp[2].element_size()),
     )
 
 
@@ -120,8 +207,7 @@ def _gated(tanh: bool) -> Workload:
     cls = GeluTanhAndMulFwdOp if tanh else GeluAndMulFwdOp
 
     def make(dev, seed):
-        g = torch.Generator(device="cpu").manual_seed(seed)
-        return (torch.randn(M, 2 * N, generator=g).to(torch.bfloat16).to(dev),)
+        return (torch.randn(M, 2 * N, generator=_gen(dev, seed), device=dev).to(torch.bfloat16),)
 
     def cpu(inp):
         from oracle import reference as ref
@@ -133,11 +219,9 @@ def _gated(tanh: bool) -> Workload:
         name=name, metric=f"achieved HBM GB/s ({cls.__name__})", unit="GB/s", dtype="bf16",
         config={"workload": f"{cls.__name__} x (4096, 22016) bf16 -> (4096, 11008) "
                             "(BASELINE configs[0])", "M": M, "N": N},
-        make_inputs=make, build_op=lambda: cls(M, N, torch.bfloat16),
-        run=lambda op, inp: op(*inp), work_per_step=lambda op: float(op.eval_roofline()[1]),
-        kernel_regex="gated_vec", cpu_fn=cpu,
-        cpu_slice=lambda inp, rows: (inp[0][:rows],),
-        cpu_units=lambda inp: 3.0 * inp[0].shape[0] * (inp[0].shape[1] // 2) * 2,
+        make_inputs=make, build_op=lambda inp: cls(inp[0].shape[0], N, torch.bfloat16),
+        run=lambda op, inp: op(*inp), work=lambda op: float(op.eval_roofline()[1]),
+        kernel_regex="gated_vec", cpu_ref=cpu, shard=_rows_shard(1), shard_desc="rows of M",
     )
 
 
@@ -145,47 +229,55 @@ def _unary(kind: str) -> Workload:
     from tileops.ops import elementwise as E
 
     shape = (16384, 16384)
-    n = shape[0] * shape[1]
     dtype = torch.int32 if kind == "bitwise_not" else torch.bfloat16
     op_cls = {"hardswish": E.HardswishFwdOp, "hardsigmoid": E.HardsigmoidFwdOp,
               "clamp_scalar": E.ClampScalarFwdOp, "isnan": E.IsnanFwdOp,
               "isinf": E.IsinfFwdOp, "isfinite": E.IsfiniteFwdOp,
               "bitwise_not": E.BitwiseNotFwdOp}[kind]
 
-    def build():
+    def build(inp):
+        n = inp[0].numel()
         if kind == "clamp_scalar":
             return op_cls(n, dtype, min=-0.5, max=0.5)
         return op_cls(n, dtype)
 
     def make(dev, seed):
-        g = torch.Generator(device="cpu").manual_seed(seed)
+        g = _gen(dev, seed)
         if dtype == torch.int32:
-            x = torch.randint(-128, 128, shape, generator=g, dtype=torch.int32)
-        else:
-            x = torch.randn(shape, generator=g).to(dtype)
-            if kind.startswith("is"):
-                q = n // 4
-                f = x.view(-1)
-                f[:q], f[q : 2 * q], f[2 * q : 3 * q] = float("nan"), float("inf"), float("-inf")
-        return (x.to(dev),)
+            return (torch.randint(-128, 128, shape, generator=g, device=dev, dtype=torch.int32),)
+        x = torch.randn(shape, generator=g, device=dev).to(dtype)
+        if kind.startswith("is"):
+            # The reference's quarter draw (workloads/elementwise.py:103-111).
+            q = x.numel() // 4
+            f = x.view(-1)
+            f[:q], f[q : 2 * q], f[2 * q : 3 * q] = float("nan"), float("inf"), float("-inf")
+        return (x,)
 
     def cpu(inp):
-        from oracle import reference as ref
+        # The reference tests' own torch programs (test_<op>.py ref_program).
+        import torch.nn.functional as F
 
-        fn = getattr(ref, kind)
-        return fn(inp[0], -0.5, 0.5) if kind == "clamp_scalar" else fn(inp[0])
+        x = inp[0]
+        if kind == "hardswish":
+            return F.hardswish(x.float()).to(dtype)
+        if kind == "hardsigmoid":
+            return F.hardsigmoid(x.float()).to(dtype)
+        if kind == "clamp_scalar":
+            return torch.clamp(x.float(), -0.5, 0.5).to(dtype)
+        if kind == "bitwise_not":
+            return torch.bitwise_not(x)
+        return getattr(torch, kind)(x.float())
 
-    out_b = 1 if kind.startswith("is") else dtype.itemsize
     return Workload(
         name=kind, metric=f"achieved HBM GB/s ({op_cls.__name__})", unit="GB/s",
         dtype=str(dtype).split(".")[-1],
-        config={"workload": f"{op_cls.__name__} [16384, 16384] {str(dtype).split('.')[-1]}"},
+        config={"workload": f"{op_cls.__name__} [16384, 16384] {str(dtype).split('.')[-1]}"
+                + (" (a quarter each NaN, +Inf, -Inf, randn)" if kind.startswith("is") else "")},
         make_inputs=make, build_op=build, run=lambda op, inp: op(*inp),
-        work_per_step=lambda op: float(op.eval_roofline()[1]),
+        work=lambda op: float(op.eval_roofline()[1]),
         kernel_regex="predicate_vec" if kind.startswith("is") else
         ("xor_stream_vec" if kind == "bitwise_not" else "unary_map_vec"),
-        cpu_fn=cpu, cpu_slice=lambda inp, rows: (inp[0][:rows],),
-        cpu_units=lambda inp: float(inp[0].numel() * (dtype.itemsize + out_b)),
+        cpu_ref=cpu, shard=_rows_shard(1), shard_desc="rows of the [16384, 16384] input",
     )
 
 
@@ -195,11 +287,11 @@ def _causal_conv(activation) -> Workload:
     B, D, L, K = 8, 4096, 8192, 4
 
     def make(dev, seed):
-        g = torch.Generator(device="cpu").manual_seed(seed)
-        x = torch.randn(B, D, L, generator=g).to(torch.bfloat16)
-        w = (0.5 * torch.randn(D, K, generator=g)).to(torch.bfloat16)
-        b = (0.1 * torch.randn(D, generator=g)).to(torch.bfloat16)
-        return tuple(t.to(dev) for t in (x, w, b))
+        g = _gen(dev, seed)
+        x = torch.randn(B, D, L, generator=g, device=dev).to(torch.bfloat16)
+        w = (0.5 * torch.randn(D, K, generator=g, device=dev)).to(torch.bfloat16)
+        b = (0.1 * torch.randn(D, generator=g, device=dev)).to(torch.bfloat16)
+        return x, w, b
 
     def cpu(inp):
         from oracle import reference as ref
@@ -211,12 +303,13 @@ def _causal_conv(activation) -> Workload:
         metric="achieved HBM GB/s (CausalDepthwiseConv1dFwdOp)", unit="GB/s", dtype="bf16",
         config={"workload": f"causal depthwise conv1d x (8, 4096, 8192) bf16, w (4096, 4), "
                             f"bias, left pad 3, activation={activation} (BASELINE configs[2])"},
-        make_inputs=make, build_op=lambda: CausalDepthwiseConv1dFwdOp(activation=activation),
-        run=lambda op, inp: op(*inp), work_per_step=lambda op: float(op.eval_roofline()[1]),
-        kernel_regex="dwconv_packet", cpu_fn=cpu,
-        cpu_slice=lambda inp, rows: (inp[0][:1, : max(rows // 64, 1)],
-                                     inp[1][: max(rows // 64, 1)], inp[2][: max(rows // 64, 1)]),
-        cpu_units=lambda inp: 2.0 * inp[0].numel() * 2 + inp[1].numel() * 2 + inp[2].numel() * 2,
+        make_inputs=make,
+        build_op=lambda inp: CausalDepthwiseConv1dFwdOp(activation=activation),
+        run=lambda op, inp: op(*inp), work=lambda op: float(op.eval_roofline()[1]),
+        kernel_regex="dwconv_packet", cpu_ref=cpu, shard=_rows_shard(1), shard_desc="batch",
+        units=lambda inp: (2 * inp[0].numel() * inp[0].element_size()
+                           + inp[1].numel() * inp[1].element_size()
+                           + inp[2].numel() * inp[2].element_size()),
     )
 
 
@@ -226,23 +319,14 @@ def _mha(causal: bool) -> Workload:
     B, S, H, D = 8, 4096, 32, 128
 
     def make(dev, seed):
-        g = torch.Generator(device="cpu").manual_seed(seed)
-        return tuple(torch.randn(B, S, H, D, generator=g).to(torch.bfloat16).to(dev)
+        g = _gen(dev, seed)
+        return tuple(torch.randn(B, S, H, D, generator=g, device=dev).to(torch.bfloat16)
                      for _ in range(3))
 
     def cpu(inp):
         from oracle import reference as ref
 
-        return ref.gqa_prefill_fwd(*inp, causal)
-
-    def sample(inp, rows):
-        s = max(128, min(S, rows * 4))
-        return tuple(t[:1, :s, :1].contiguous() for t in inp)
-
-    def units(inp):
-        s = inp[0].shape[1]
-        f = 4.0 * s * s * D
-        return f / 2 if causal else f
+        return ref.mha_sdpa(*inp, causal)
 
     return Workload(
         name="mha_causal" if causal else "mha", unit="TFLOP/s", dtype="bf16", bound="tensor",
@@ -250,9 +334,11 @@ def _mha(causal: bool) -> Workload:
         config={"workload": f"MultiHeadAttentionFwdOp q/k/v (8, 4096, 32, 128) bf16 BSHD, "
                             f"causal={causal}, scale 1/sqrt(128) (BASELINE configs[3])"},
         make_inputs=make,
-        build_op=lambda: MultiHeadAttentionFwdOp(B, H, S, D, causal, torch.bfloat16),
-        run=lambda op, inp: op(*inp), work_per_step=lambda op: float(op.eval_roofline()[0]),
-        kernel_regex="attn_fwd_kernel", cpu_fn=cpu, cpu_slice=sample, cpu_units=units,
+        build_op=lambda inp: MultiHeadAttentionFwdOp(inp[0].shape[0], H, S, D, causal,
+                                                     torch.bfloat16),
+        run=lambda op, inp: op(*inp), work=lambda op: float(op.eval_roofline()[0]),
+        kernel_regex="attn_fwd_kernel", cpu_ref=cpu, shard=_rows_shard(3),
+        shard_desc="batch ((batch, head) pairs)",
     )
 
 
@@ -264,39 +350,42 @@ def _gdn() -> Workload:
     B, T, H, DK, DV = 4, 8192, 16, 128, 128
 
     def make(dev, seed):
-        g_ = torch.Generator(device="cpu").manual_seed(seed)
-        q = F.normalize(torch.randn(B, T, H, DK, generator=g_), dim=-1).to(torch.bfloat16)
-        k = F.normalize(torch.randn(B, T, H, DK, generator=g_), dim=-1).to(torch.bfloat16)
-        v = torch.randn(B, T, H, DV, generator=g_).to(torch.bfloat16)
-        g = F.logsigmoid(torch.randn(B, T, H, generator=g_)) / 16
-        beta = torch.sigmoid(torch.randn(B, T, H, generator=g_))
-        return tuple(t.to(dev) for t in (q, k, v, g, beta))
+        g_ = _gen(dev, seed)
+        q = F.normalize(torch.randn(B, T, H, DK, generator=g_, device=dev), dim=-1)
+        k = F.normalize(torch.randn(B, T, H, DK, generator=g_, device=dev), dim=-1)
+        v = torch.randn(B, T, H, DV, generator=g_, device=dev)
+        g = F.logsigmoid(torch.randn(B, T, H, generator=g_, device=dev)) / 16
+        beta = torch.sigmoid(torch.randn(B, T, H, generator=g_, device=dev))
+        return (q.to(torch.bfloat16), k.to(torch.bfloat16), v.to(torch.bfloat16), g, beta)
+
+    def shard(inp, index, count):
+        sl = bh_split(B, H, index, count)
+        if sl is None:
+            return None
+        bs, hs = sl
+        return tuple(t[bs, :, hs].contiguous() for t in inp)
+
+    def unshard(flats, count):
+        return [unshard_bthd(flats[0], B, T, H, DV, count), flats[1].view(B, H, DK, DV)]
 
     def cpu(inp):
         from oracle import reference as ref
 
         return ref.gdn_prefill_bthd(*inp)
 
-    def sample(inp, rows):
-        t = max(64, min(T, rows * 4))
-        return tuple(x[:1, :t, :1].contiguous() for x in inp)
-
-    def units(inp):
-        t = inp[0].shape[1]
-        return float(t * (4 * 64 * DK + 6 * DK * DV + 3 * 64 * DV))
-
     return Workload(
         name="gdn", unit="TFLOP/s", dtype="bf16", bound="hbm", roof_unit="GB/s",
-        roof_work_per_step=lambda op: float(op.eval_roofline()[1]),
+        roof_work=lambda op: float(op.eval_roofline()[1]),
         metric="achieved TFLOP/s (GatedDeltaNetPrefillFwdOp)",
         config={"workload": "GatedDeltaNetPrefillFwdOp B=4 T=8192 H=16 dk=dv=128 chunk 64, "
                             "q/k L2-normalised, g=logsigmoid(N)/16, beta=sigmoid(N), h0=0 "
                             "(BASELINE configs[4])"},
         make_inputs=make,
-        build_op=lambda: GatedDeltaNetPrefillFwdOp(B, T, H, DK, DV),
-        run=lambda op, inp: op(*inp), work_per_step=lambda op: float(op.eval_roofline()[0]),
-        kernel_regex="gdn_", cpu_fn=cpu, cpu_slice=sample, cpu_units=units,
-        launches_per_step=2,  # gdn_prepare + gdn_scan
+        build_op=lambda inp: GatedDeltaNetPrefillFwdOp(inp[0].shape[0], T, inp[0].shape[2],
+                                                       DK, DV),
+        run=lambda op, inp: op(*inp), work=lambda op: float(op.eval_roofline()[0]),
+        kernel_regex="gdn_", cpu_ref=cpu, shard=shard, unshard=unshard,
+        shard_desc="(batch, head) pairs", launches_per_call=2,  # gdn_prepare + gdn_scan
     )
 
 
@@ -306,32 +395,28 @@ def _gla() -> Workload:
     B, H, DK, DV = 8, 32, 128, 128
 
     def make(dev, seed):
-        g = torch.Generator(device="cpu").manual_seed(seed)
-        q = torch.randn(B, H, DK, generator=g) * 0.5
-        k = torch.randn(B, H, DK, generator=g) * 0.5
-        v = torch.randn(B, H, DV, generator=g) * 0.5
-        gk = -torch.rand(B, H, DK, generator=g)
-        state = torch.randn(B, H, DK, DV, generator=g)
-        return tuple(t.to(torch.bfloat16).to(dev) for t in (q, k, v, gk, state))
+        g = _gen(dev, seed)
+        q = torch.randn(B, H, DK, generator=g, device=dev) * 0.5
+        k = torch.randn(B, H, DK, generator=g, device=dev) * 0.5
+        v = torch.randn(B, H, DV, generator=g, device=dev) * 0.5
+        gk = -torch.rand(B, H, DK, generator=g, device=dev)
+        state = torch.randn(B, H, DK, DV, generator=g, device=dev)
+        return tuple(t.to(torch.bfloat16) for t in (q, k, v, gk, state))
 
     def cpu(inp):
         from oracle import reference as ref
 
         return ref.gla_decode(*inp, DK ** -0.5)
 
-    def units(inp):
-        b, h = inp[0].shape[:2]
-        return float(b * h * (3 * DK + 2 * DV + 2 * DK * DV) * 2)
-
     return Workload(
         name="gla_decode", metric="achieved HBM GB/s (GLADecodeOp)", unit="GB/s",
-        dtype="bf16",
+        dtype="bf16", baseline=False,
         config={"workload": "GLADecodeOp B=8 H=32 DK=DV=128 bf16, one decode step (the "
                             "reference test's largest serving case, serving-b8-h32)"},
-        make_inputs=make, build_op=lambda: GLADecodeOp(B, H, DK, DV, dtype=torch.bfloat16),
-        run=lambda op, inp: op(*inp), work_per_step=lambda op: float(op.eval_roofline()[1]),
-        kernel_regex="gla_decode", cpu_fn=cpu,
-        cpu_slice=lambda inp, rows: tuple(t[:1] for t in inp), cpu_units=units,
+        make_inputs=make,
+        build_op=lambda inp: GLADecodeOp(inp[0].shape[0], H, DK, DV, dtype=torch.bfloat16),
+        run=lambda op, inp: op(*inp), work=lambda op: float(op.eval_roofline()[1]),
+        kernel_regex="gla_decode", cpu_ref=cpu, shard=_rows_shard(5), shard_desc="batch",
     )
 
 
@@ -342,40 +427,36 @@ def _ssd() -> Workload:
     S = NC * Q
 
     def make(dev, seed):
-        g = torch.Generator(device="cpu").manual_seed(seed)
-        x = (torch.randn(B, S, H, P, generator=g) * 0.1).to(torch.bfloat16)
-        cb = (torch.randn(B, NC, G, Q, Q, generator=g) * 0.1).to(torch.bfloat16)
-        dA = -torch.rand(B, H, NC, Q, generator=g).cumsum(-1)
-        Cm = (torch.randn(B, S, G, N, generator=g) * 0.1).to(torch.bfloat16)
-        prev = torch.randn(B, NC, H, P, N, generator=g) * 0.1
-        dt = (torch.rand(B, H, NC, Q, generator=g) * 0.1 + 0.01).to(torch.bfloat16)
-        return tuple(t.to(dev) for t in (x, cb, dA, Cm, prev, dt))
+        g = _gen(dev, seed)
+        x = (torch.randn(B, S, H, P, generator=g, device=dev) * 0.1).to(torch.bfloat16)
+        cb = (torch.randn(B, NC, G, Q, Q, generator=g, device=dev) * 0.1).to(torch.bfloat16)
+        dA = -torch.rand(B, H, NC, Q, generator=g, device=dev).cumsum(-1)
+        Cm = (torch.randn(B, S, G, N, generator=g, device=dev) * 0.1).to(torch.bfloat16)
+        prev = torch.randn(B, NC, H, P, N, generator=g, device=dev) * 0.1
+        dt = (torch.rand(B, H, NC, Q, generator=g, device=dev) * 0.1 + 0.01).to(torch.bfloat16)
+        return x, cb, dA, Cm, prev, dt
 
     def cpu(inp):
         from oracle import reference as ref
 
         return ref.ssd_chunk_scan(*inp, G)
 
-    def sample(inp, rows):  # one chunk of batch 0, all heads
+    def units(inp):  # the op's eval_roofline bytes from the input shapes
         x, cb, dA, Cm, prev, dt = inp
-        return (x[:1, :Q], cb[:1, :1], dA[:1, :, :1], Cm[:1, :Q], prev[:1, :1], dt[:1, :, :1])
-
-    def units(inp):  # bytes of the sample by the op's formula
-        x, cb, dA, Cm, prev, dt = inp
-        b, s, h, pp = x.shape
-        tok = b * s * h
-        return float(tok * pp * 2 + cb.numel() * 2 + tok * 4 + Cm.numel() * 2 + prev.numel() * 4
-                     + tok * 2 + tok * pp * 4)
+        b, s, h, p = x.shape
+        tok, eb = b * s * h, x.element_size()
+        return float(tok * p * eb + cb.numel() * eb + tok * 4 + Cm.numel() * eb
+                     + prev.numel() * 4 + tok * eb + tok * p * 4)
 
     return Workload(
         name="ssd_chunk_scan", metric="achieved HBM GB/s (SSDChunkScanFwdOp)", unit="GB/s",
-        dtype="bf16",
+        dtype="bf16", baseline=False,
         config={"workload": "SSDChunkScanFwdOp x (4, 2048, 80, 64) bf16, chunk 256, d_state "
                             "128, 1 group (manifest mamba2-2p7b-b4-s2k)"},
-        make_inputs=make, build_op=SSDChunkScanFwdOp,
-        run=lambda op, inp: op(*inp),
-        work_per_step=lambda op: float(op.eval_roofline()[1]),
-        kernel_regex="ssd_chunk_scan", cpu_fn=cpu, cpu_slice=sample, cpu_units=units,
+        make_inputs=make, build_op=lambda inp: SSDChunkScanFwdOp(),
+        run=lambda op, inp: op(*inp), work=lambda op: float(op.eval_roofline()[1]),
+        kernel_regex="ssd_chunk_scan", cpu_ref=cpu, shard=_rows_shard(6), shard_desc="batch",
+        units=units,
     )
 
 
@@ -385,33 +466,28 @@ def _conv_dense() -> Workload:
     N, CI, L, CO, K = 1, 80, 3000, 1280, 3
 
     def make(dev, seed):
-        g = torch.Generator(device="cpu").manual_seed(seed)
-        x = torch.randn(N, CI, L, generator=g).to(torch.float16)
-        w = (torch.randn(CO, CI, K, generator=g) * 0.1).to(torch.float16)
-        b = (torch.randn(CO, generator=g) * 0.1).to(torch.float16)
-        return tuple(t.to(dev) for t in (x, w, b))
+        g = _gen(dev, seed)
+        x = torch.randn(N, CI, L, generator=g, device=dev).to(torch.float16)
+        w = (torch.randn(CO, CI, K, generator=g, device=dev) * 0.1).to(torch.float16)
+        b = (torch.randn(CO, generator=g, device=dev) * 0.1).to(torch.float16)
+        return x, w, b
 
     def cpu(inp):
         from oracle import reference as ref
 
         return ref.conv1d(inp[0], inp[1], inp[2], 1, 0, 1, 1)
 
-    def sample(inp, rows):  # a slice of the output channels
-        co = max(8, min(CO, rows))
-        return (inp[0], inp[1][:co], inp[2][:co])
-
-    def units(inp):
-        co = inp[1].shape[0]
-        return float(2 * N * co * CI * (L - K + 1) * K)
-
     return Workload(
-        name="conv1d_dense", unit="TFLOP/s", dtype="f16", bound="tensor",
+        name="conv1d_dense", unit="TFLOP/s", dtype="f16", bound="tensor", baseline=False,
         metric="achieved TFLOP/s (Conv1dBiasFwdOp, dense)",
         config={"workload": "Conv1dBiasFwdOp x (1, 80, 3000) f16, weight (1280, 80, 3), bias, "
                             "stride 1, no padding (manifest whisper-conv1-bias)"},
-        make_inputs=make, build_op=lambda: Conv1dBiasFwdOp(),
-        run=lambda op, inp: op(*inp), work_per_step=lambda op: float(op.eval_roofline()[0]),
-        kernel_regex="conv1d_igemm", cpu_fn=cpu, cpu_slice=sample, cpu_units=units,
+        make_inputs=make, build_op=lambda inp: Conv1dBiasFwdOp(),
+        run=lambda op, inp: op(*inp), work=lambda op: float(op.eval_roofline()[0]),
+        kernel_regex="conv1d_igemm", cpu_ref=cpu, shard=None,
+        # 2 flops per tap (valid padding: every one of the K taps of every
+        # output is in range) + 1 per output for the bias.
+        units=lambda inp: float(N * CO * (L - K + 1) * (2 * CI * K + 1)),
     )
 
 
@@ -428,43 +504,40 @@ def _gdn_varlen() -> Workload:
     offsets = [0] + cuts + [TOTAL]
 
     def make(dev, seed):
-        g_ = torch.Generator(device="cpu").manual_seed(seed)
-        q = F.normalize(torch.randn(1, TOTAL, H, DK, generator=g_), dim=-1).to(torch.bfloat16)
-        k = F.normalize(torch.randn(1, TOTAL, H, DK, generator=g_), dim=-1).to(torch.bfloat16)
-        v = torch.randn(1, TOTAL, H, DV, generator=g_).to(torch.bfloat16)
-        g = F.logsigmoid(torch.randn(1, TOTAL, H, generator=g_)) / 16
-        beta = torch.sigmoid(torch.randn(1, TOTAL, H, generator=g_))
-        cu = torch.tensor(offsets, dtype=torch.int32)
-        return tuple(t.to(dev) for t in (q, k, v, g, beta, cu))
+        g_ = _gen(dev, seed)
+        q = F.normalize(torch.randn(1, TOTAL, H, DK, generator=g_, device=dev), dim=-1)
+        k = F.normalize(torch.randn(1, TOTAL, H, DK, generator=g_, device=dev), dim=-1)
+        v = torch.randn(1, TOTAL, H, DV, generator=g_, device=dev)
+        g = F.logsigmoid(torch.randn(1, TOTAL, H, generator=g_, device=dev)) / 16
+        beta = torch.sigmoid(torch.randn(1, TOTAL, H, generator=g_, device=dev))
+        cu = torch.tensor(offsets, dtype=torch.int32, device=dev)
+        return (q.to(torch.bfloat16), k.to(torch.bfloat16), v.to(torch.bfloat16), g, beta, cu)
 
     def cpu(inp):
         from oracle import reference as ref
 
         return ref.gdn_prefill_varlen(*inp[:5], inp[5])
 
-    def sample(inp, rows):  # the first sequence's first tokens, one head
-        t = max(64, min(offsets[1], rows * 4))
-        return tuple(x[:1, :t, :1].contiguous() for x in inp[:5]) + (
+    def sample(inp):  # the first sequence, all heads
+        t = offsets[1]
+        return tuple(x[:, :t].contiguous() for x in inp[:5]) + (
             torch.tensor([0, t], dtype=torch.int32),)
-
-    def units(inp):
-        t = inp[0].shape[1]
-        return float(t * (4 * 64 * DK + 6 * DK * DV + 3 * 64 * DV))
 
     return Workload(
         name="gdn_varlen", unit="TFLOP/s", dtype="bf16", bound="hbm", roof_unit="GB/s",
-        roof_work_per_step=lambda op: float(op.eval_roofline()[1]),
+        roof_work=lambda op: float(op.eval_roofline()[1]), baseline=False,
         metric="achieved TFLOP/s (GatedDeltaNetPrefillFwdOp, packed cu_seqlens)",
         config={"workload": "GatedDeltaNetPrefillFwdOp packed: 32768 tokens (the BASELINE "
                             "token count) in 12 seeded ragged sequences, H=16 dk=dv=128, "
                             "chunk 64, same input distributions as the BASELINE config",
                 "cu_seqlens": offsets},
         make_inputs=make,
-        build_op=lambda: GatedDeltaNetPrefillFwdOp(1, TOTAL, H, DK, DV),
+        build_op=lambda inp: GatedDeltaNetPrefillFwdOp(1, inp[0].shape[1], H, DK, DV),
         run=lambda op, inp: op(*inp[:5], None, cu_seqlens=inp[5]),
-        work_per_step=lambda op: float(op.eval_roofline()[0]),
-        kernel_regex="gdn_", cpu_fn=cpu, cpu_slice=sample, cpu_units=units,
-        launches_per_step=3,  # chunk index + prepare + scan
+        work=lambda op: float(op.eval_roofline()[0]),
+        kernel_regex="gdn_", cpu_ref=cpu, cpu_sample=sample,
+        cpu_sample_desc=f"the first packed sequence ({offsets[1]} tokens, all 16 heads)",
+        shard=None, launches_per_call=3,  # chunk index + prepare + scan
     )
 
 
@@ -473,6 +546,11 @@ def workloads() -> dict[str, Callable[[], Workload]]:
         "fused_add_layer_norm": _faln,
         "gelu_and_mul": lambda: _gated(False),
         "gelu_tanh_and_mul": lambda: _gated(True),
+    }
+    for kind in ("hardswish", "hardsigmoid", "clamp_scalar", "isnan", "isinf", "isfinite",
+                 "bitwise_not"):
+        table[kind] = (lambda k: (lambda: _unary(k)))(kind)
+    table.update({
         "causal_conv1d": lambda: _causal_conv(None),
         "causal_conv1d_silu": lambda: _causal_conv("silu"),
         "mha": lambda: _mha(False),
@@ -482,10 +560,7 @@ def workloads() -> dict[str, Callable[[], Workload]]:
         "gla_decode": _gla,
         "ssd_chunk_scan": _ssd,
         "conv1d_dense": _conv_dense,
-    }
-    for kind in ("hardswish", "hardsigmoid", "clamp_scalar", "isnan", "isinf", "isfinite",
-                 "bitwise_not"):
-        table[kind] = (lambda k: (lambda: _unary(k)))(kind)
+    })
     return table
 
 
@@ -501,7 +576,8 @@ def load_peaks() -> tuple[dict, str]:
 
 
 def load_traffic(name: str) -> Optional[float]:
-    """DRAM bytes per launch of the op's dominant kernel from the committed ncu summary."""
+    """DRAM bytes per launch of the op's dominant kernel from the committed
+    ncu summary (a static capture, not a measurement of this run)."""
     path = ROOT / "profiles" / "ncu_traffic.json"
     if not path.exists():
         return None
@@ -565,6 +641,7 @@ class ClockSampler:
 
     def __enter__(self):
         if self._nvml is not None:
+            self._stop.clear()
             self._thread = threading.Thread(target=self._loop, daemon=True)
             self._thread.start()
         return self
@@ -573,6 +650,7 @@ class ClockSampler:
         self._stop.set()
         if self._thread is not None:
             self._thread.join()
+            self._thread = None
             try:
                 self._sample()
             except Exception:
@@ -616,84 +694,393 @@ def barrier(world: int, device) -> None:
             dist.barrier()
 
 
-def gather_outputs(outs, world: int, device, reps: int = 5):
+def check_shard_shapes(shapes: list[tuple], world: int, device) -> None:
+    """Every rank must hold shards of the same shapes before an all-gather
+    (``all_gather_into_tensor`` needs equal sizes): exchange the shapes and
+    raise on every rank, naming the ranks, if they differ."""
+    if world == 1:
+        return
+    import torch.distributed as dist
+
+    flat = [len(shapes)] + [len(s) for s in shapes] + [d for s in shapes for d in s]
+    width = torch.tensor([len(flat)], dtype=torch.int64, device=device)
+    widths = [torch.zeros_like(width) for _ in range(world)]
+    dist.all_gather(widths, width)
+    n = int(max(w.item() for w in widths))
+    mine = torch.full((n,), -1, dtype=torch.int64, device=device)
+    mine[: len(flat)] = torch.tensor(flat, dtype=torch.int64, device=device)
+    every = [torch.empty_like(mine) for _ in range(world)]
+    dist.all_gather(every, mine)
+    ref = every[0]
+    bad = [r for r in range(world) if not torch.equal(every[r], ref)]
+    if bad:
+        raise RuntimeError(f"shard shapes differ between rank 0 and ranks {bad}: "
+                           f"{[e.tolist() for e in every]}")
+
+
+def gather_outputs(outs, world: int, device, fulls=None):
     """Reassemble every rank's output shards on every rank: one
-    ``all_gather_into_tensor`` per output tensor (NCCL over NVLink on GPUs,
-    gloo on CPU ranks).  It moves results only -- no op needs data from
-    another rank -- so it is timed apart from the op: the mean of ``reps``
-    rounds, the max over ranks.  Returns (summary, gathered tensors)."""
+    ``all_gather_into_tensor`` per output (NCCL over NVLink on GPUs, gloo
+    on CPU ranks), into ``fulls`` (allocated when None).  Shards land in
+    rank order.  Returns the gathered flat tensors."""
     import torch.distributed as dist
 
     flats = [o.contiguous().view(-1) for o in outs]
-    fulls = [torch.empty(world * f.numel(), dtype=f.dtype, device=f.device) for f in flats]
-
-    def one_round():
-        for full, flat in zip(fulls, flats):
-            dist.all_gather_into_tensor(full, flat)
-
-    one_round()  # warm-up; its result is what the caller checks
-    barrier(world, device)
-    if device.type == "cuda":
-        torch.cuda.synchronize(device)
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record(torch.cuda.current_stream(device))
-        for _ in range(reps):
-            one_round()
-        e1.record(torch.cuda.current_stream(device))
-        torch.cuda.synchronize(device)
-        ms = e0.elapsed_time(e1) / reps
-    else:
-        t0 = time.perf_counter()
-        for _ in range(reps):
-            one_round()
-        ms = (time.perf_counter() - t0) * 1e3 / reps
-    ms = max_over_ranks(ms, world, device)
-    per_rank = sum(f.numel() * f.element_size() for f in flats)
-    total = world * per_rank
-    summary = {
-        "collective": "all_gather_into_tensor (output reassembly only)",
-        "outputs": len(flats), "bytes_per_rank": per_rank, "bytes_total": total,
-        "bytes_received_per_rank": (world - 1) * per_rank, "ms": ms,
-        "algbw_GBps": total / (ms * 1e-3) / 1e9,
-        "busbw_GBps": (world - 1) / world * total / (ms * 1e-3) / 1e9,
-    }
-    return summary, fulls
+    if fulls is None:
+        fulls = [torch.empty(world * f.numel(), dtype=f.dtype, device=f.device) for f in flats]
+    for full, flat in zip(fulls, flats):
+        dist.all_gather_into_tensor(full, flat)
+    return fulls
 
 
-def whole_job_value(work_per_step: float, steps: int, total_ms: float, world: int,
-                    unit: str) -> float:
-    """Weak scaling: every rank ran ``steps`` steps of ``work_per_step`` units;
-    ``total_ms`` is the slowest rank's timed region."""
+def whole_job_value(work_per_step: float, steps: int, total_ms: float, unit: str) -> float:
+    """Throughput of ``steps`` steps of ``work_per_step`` units (summed over
+    ranks) in ``total_ms`` (the slowest rank's timed region)."""
     scale = 1e9 if unit == "GB/s" else 1e12
-    return world * work_per_step * steps / (total_ms * 1e-3) / scale
+    return work_per_step * steps / (total_ms * 1e-3) / scale
 
 
-# ---------------------------------------------------------------- our arm
-def time_cpu_baseline(wl: Workload, budget_s: float = 8.0) -> dict:
-    """The oracle (the reference's torch CPU ref program) on a bounded sample."""
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    full = wl.make_inputs(torch.device("cpu"), 1235)
-    rows = 256
-    sample = wl.cpu_slice(full, rows)
-    wl.cpu_fn(sample)  # warm-up
+def _nbytes(ts) -> int:
+    return sum(t.numel() * t.element_size() for t in ts if isinstance(t, torch.Tensor))
+
+
+def _as_tuple(out) -> tuple:
+    return tuple(out) if isinstance(out, (tuple, list)) else (out,)
+
+
+def _problem(wl: Workload, device, seed: int, rank: int, world: int) -> tuple:
+    """The rank's part of the problem drawn from ``seed``: the whole problem
+    at N = 1, else the rank's shard of the same full problem."""
+    full = wl.make_inputs(device, seed)
+    if world == 1:
+        return full
+    mine = wl.shard(full, rank, world) if wl.shard else None
+    if mine is None:
+        raise RuntimeError(f"{wl.name}: the problem does not split into {world} equal shards")
+    del full
+    return mine
+
+
+# -------------------------------------------------------------- timing legs
+def time_calls(wl: Workload, op, sets: list, steps: int, warmup: int, graph: bool,
+               device, stream) -> dict:
+    """K op calls over rotating input sets: graph replays (or eager calls)
+    with CUDA events around each; returns total and mean per-call ms."""
+    n_sets = len(sets)
+    for i in range(warmup):
+        wl.run(op, sets[i % n_sets])
+    torch.cuda.synchronize(device)
+    out_bytes = max(1, _nbytes(_as_tuple(wl.run(op, sets[0]))))
+    per_graph = max(1, min(64, (8 << 30) // out_bytes) // n_sets) * n_sets
+    per_graph = min(per_graph, steps)
+
+    def capture(n):
+        g = torch.cuda.CUDAGraph()
+        keep = []
+        with torch.cuda.graph(g):
+            for i in range(n):
+                keep.append(wl.run(op, sets[i % n_sets]))
+        del keep
+        return g
+
+    graphs = []
+    if graph:
+        g_main = capture(per_graph)
+        graphs.append(g_main)
+        rem = steps % per_graph
+        chunks = [(g_main.replay, per_graph)] * (steps // per_graph)
+        if rem:
+            g_rem = capture(rem)
+            graphs.append(g_rem)
+            chunks.append((g_rem.replay, rem))
+        for _ in range(max(1, -(-warmup // per_graph))):
+            g_main.replay()
+        torch.cuda.synchronize(device)
+    else:
+        chunks = [((lambda inp=sets[i % n_sets]: wl.run(op, inp)), 1) for i in range(steps)]
+    starts = [torch.cuda.Event(enable_timing=True) for _ in chunks]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in chunks]
+    torch.cuda.synchronize(device)
+    for i, (fn, _) in enumerate(chunks):
+        starts[i].record(stream)
+        fn()
+        ends[i].record(stream)
+    torch.cuda.synchronize(device)
+    total = starts[0].elapsed_time(ends[-1])
+    per_call = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / steps
+    calls = chunks[0][1]
+    del chunks, graphs
+    return {"total_ms": total, "per_call_ms": per_call, "calls_per_replay": calls}
+
+
+def time_sharded_steps(wl: Workload, op, sets: list, steps: int, warmup: int, world: int,
+                       device, stream) -> dict:
+    """K steps of (op on this rank's shard, then every output gathered on
+    every rank and put back in the full layout), eager, CUDA events around
+    all K steps on the launching stream."""
+    n_sets = len(sets)
+    outs = _as_tuple(wl.run(op, sets[0]))
+    check_shard_shapes([tuple(o.shape) for o in outs], world, device)
+    fulls = gather_outputs(outs, world, device)
+
+    def step(i):
+        res = _as_tuple(wl.run(op, sets[i % n_sets]))
+        gathered = gather_outputs(res, world, device, fulls)
+        if wl.unshard is not None:
+            wl.unshard(gathered, world)
+
+    for i in range(max(1, warmup)):
+        step(i)
+    torch.cuda.synchronize(device)
+    barrier(world, device)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(steps):
+        step(i)
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    step_ms = e0.elapsed_time(e1) / steps
+    # The reassembly alone, for the breakdown.
+    barrier(world, device)
+    g0 = torch.cuda.Event(enable_timing=True)
+    g1 = torch.cuda.Event(enable_timing=True)
+    reps = max(3, min(steps, 10))
+    g0.record(stream)
+    for _ in range(reps):
+        gathered = gather_outputs(outs, world, device, fulls)
+        if wl.unshard is not None:
+            wl.unshard(gathered, world)
+    g1.record(stream)
+    torch.cuda.synchronize(device)
+    gather_ms = g0.elapsed_time(g1) / reps
+    per_rank = _nbytes(outs)
+    return {"step_ms": step_ms, "gather_ms": gather_ms, "bytes_per_rank": per_rank,
+            "bytes_total": world * per_rank, "bytes_received_per_rank": (world - 1) * per_rank}
+
+
+def time_e2e(wl: Workload, host_full: tuple, device, steps: int, max_chunks: int = 16) -> dict:
+    """The public op API from pinned host buffers, chunked so that copies in
+    both directions overlap the kernels: per chunk, H2D on one stream, the op
+    on a second, D2H of its outputs on a third.  Returns ms per step (all
+    chunks) and the bytes copied each way."""
+    n_chunks = 1
+    for c in (max_chunks, 8, 4, 2):
+        if c <= max_chunks and wl.shard is not None and wl.shard(host_full, 0, c) is not None:
+            n_chunks = c
+            break
+    if n_chunks == 1:
+        parts = [host_full]
+    else:
+        parts = [wl.shard(host_full, i, n_chunks) for i in range(n_chunks)]
+    host_in = [tuple(t.pin_memory() if isinstance(t, torch.Tensor) else t for t in p)
+               for p in parts]
+    dev_in = [tuple(torch.empty(t.shape, dtype=t.dtype, device=device)
+                    if isinstance(t, torch.Tensor) else t for t in p) for p in host_in]
+    op = wl.build_op(dev_in[0])
+    for d, h in zip(dev_in, host_in):
+        for dt, ht in zip(d, h):
+            if isinstance(dt, torch.Tensor):
+                dt.copy_(ht)
+    first = _as_tuple(wl.run(op, dev_in[0]))
+    host_out = [tuple(torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for o in first)
+                for _ in range(n_chunks)]
+    del first
+    s_in = torch.cuda.Stream(device)
+    s_comp = torch.cuda.Stream(device)
+    s_out = torch.cuda.Stream(device)
+    ev_in = [torch.cuda.Event() for _ in range(n_chunks)]
+    ev_done = [torch.cuda.Event() for _ in range(n_chunks)]
+    torch.cuda.synchronize(device)
+
+    def one_step():
+        for i in range(n_chunks):
+            with torch.cuda.stream(s_in):
+                s_in.wait_event(ev_done[i])  # the previous step's call read these buffers
+                for dt, ht in zip(dev_in[i], host_in[i]):
+                    if isinstance(dt, torch.Tensor):
+                        dt.copy_(ht, non_blocking=True)
+                ev_in[i].record(s_in)
+            with torch.cuda.stream(s_comp):
+                s_comp.wait_event(ev_in[i])
+                res = _as_tuple(wl.run(op, dev_in[i]))
+                ev_done[i].record(s_comp)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(ev_done[i])
+                for h, d in zip(host_out[i], res):
+                    d.record_stream(s_out)
+                    h.copy_(d, non_blocking=True)
+            del res
+
+    for _ in range(2):
+        one_step()
+    torch.cuda.synchronize(device)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(s_in)
+    for _ in range(steps):
+        one_step()
+    s_out.wait_stream(s_in)
+    s_out.wait_stream(s_comp)
+    e1.record(s_out)
+    torch.cuda.synchronize(device)
+    ms = e0.elapsed_time(e1) / steps
+    h2d = sum(_nbytes(h) for h in host_in)
+    d2h = sum(_nbytes(h) for h in host_out)
+    return {"ms_per_step": ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "chunks": n_chunks, "calls_per_step": n_chunks,
+            "api": f"{type(op).__name__}.__call__ per chunk, pinned host buffers, "
+                   f"H2D / op / D2H on three streams"}
+
+
+def time_cpu(fn: Callable, inputs: tuple, budget_s: float = 10.0) -> tuple[float, int, bool]:
+    """Seconds per call of ``fn(inputs)``: one call, then (when it took less
+    than half the budget) up to 3 more within the budget, reporting their
+    median.  Returns (seconds, timed calls, first call only)."""
+    t0 = time.perf_counter()
+    fn(inputs)
+    first = time.perf_counter() - t0
+    if first * 2 > budget_s:
+        return first, 1, True
     times = []
     t_end = time.perf_counter() + budget_s
-    while time.perf_counter() < t_end or len(times) < 3:
+    while len(times) < 3 and (time.perf_counter() < t_end or len(times) < 1):
         t0 = time.perf_counter()
-        wl.cpu_fn(sample)
+        fn(inputs)
         times.append(time.perf_counter() - t0)
-    med = statistics.median(times)
-    units = wl.cpu_units(sample)
-    value = units / med / (1e9 if wl.unit == "GB/s" else 1e12)
-    desc = ", ".join(f"{tuple(t.shape)}" for t in sample if isinstance(t, torch.Tensor))
-    return {"value": value, "unit": wl.unit, "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"oracle on inputs {desc}, median of {len(times)} reps ({med*1e3:.2f} ms)",
+    return statistics.median(times), len(times), False
+
+
+def cpu_baseline(wl: Workload, full_cpu: tuple, work: float, budget_s: float = 10.0) -> dict:
+    """The reference's torch CPU program on all host threads: the full
+    configuration, or the workload's stated sample when it has one."""
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    if wl.cpu_sample is not None:
+        inputs = wl.cpu_sample(full_cpu)
+        units = host_work(wl, inputs)
+        desc = f"sample: {wl.cpu_sample_desc}"
+        same = False
+    else:
+        inputs, units, desc, same = full_cpu, work, "the full configuration", True
+    sec, reps, cold = time_cpu(lambda inp: wl.cpu_ref(inp), inputs, budget_s)
+    scale = 1e9 if wl.unit == "GB/s" else 1e12
+    return {"value": units / sec / scale, "unit": wl.unit, "cores": torch.get_num_threads(),
+            "kind": "port", "same_config": same, "ms_per_call": sec * 1e3,
+            "sample": f"reference torch CPU program (restated in oracle/) on {desc}; "
+                      + ("one cold call" if cold else f"median of {reps} calls after one"),
             "cpu_count": os.cpu_count()}
 
 
-def run_ours(args, wl: Workload) -> Optional[dict]:
+# ------------------------------------------------------------------ our arm
+def _peak(unit: str, peaks: dict) -> tuple[float, str]:
+    if unit == "GB/s":
+        return float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])), "GB/s"
+    return float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])), "TFLOP/s"
+
+
+def measure(wl: Workload, args, rank: int, local_rank: int, world: int, device,
+            with_cpu: bool, headline: bool) -> dict:
+    """Every leg of one op: kernel-only replays, the sharded step with its
+    reassembly (N > 1), the end-to-end host path, and the CPU baseline."""
+    stream = torch.cuda.current_stream(device)
+    probe = _problem(wl, device, SEED, rank, world)
+    op = wl.build_op(probe)
+    set_bytes = _nbytes(probe) + _nbytes(_as_tuple(wl.run(op, probe)))
+    n_sets = max(2, min(32, -(-3 * L2_BYTES // max(set_bytes, 1)) + 1))
+    sets = [probe] + [_problem(wl, device, SEED + 1000 * i, rank, world)
+                      for i in range(1, n_sets)]
+    work = wl.work(op)  # one call on this rank's part
+    peaks, peak_kind = load_peaks()
+    roof_unit = wl.roof_unit or wl.unit
+    roof_work = wl.roof_work(op) if wl.roof_work else work
+    peak, peak_unit = _peak(roof_unit, peaks)
+    steps = args.steps if headline else min(args.steps, args.per_op_steps)
+
+    sampler = ClockSampler(local_rank)
+    barrier(world, device)
+    with sampler:
+        k = time_calls(wl, op, sets, steps, args.warmup, args.graph, device, stream)
+        sharded = None
+        if world > 1:
+            sharded = time_sharded_steps(wl, op, sets, steps, args.warmup, world, device,
+                                         stream)
+    barrier(world, device)
+    per_call_ms = max_over_ranks(k["per_call_ms"], world, device)
+    total_ms = max_over_ranks(k["total_ms"], world, device)
+    achieved = roof_work / (per_call_ms * 1e-3) / (1e9 if roof_unit == "GB/s" else 1e12)
+    rec = {
+        "metric": wl.metric, "unit": wl.unit, "dtype": wl.dtype, "config": dict(wl.config),
+        "roofline": {"bound": wl.bound, "achieved": achieved, "peak": peak, "unit": peak_unit,
+                     "frac": achieved / peak, "traffic": load_traffic(wl.name),
+                     "traffic_source": "profiles/ncu_traffic.json (static ncu capture of "
+                                       "this workload, not this run)",
+                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json)"
+                     if peak_kind == "measured" else "fallback",
+                     "per_launch_ms": per_call_ms, "algorithmic_per_launch": roof_work},
+        "l2": f"rotating {n_sets} input/output sets ({n_sets * set_bytes / 2**20:.0f} MiB) "
+              "> 126 MB L2",
+        "timing": (f"CUDA-graph replays of {k['calls_per_replay']} op calls each, CUDA events "
+                   "around each replay" if args.graph else "eager op calls"),
+    }
+    if world == 1:
+        rec["value"] = whole_job_value(work, steps, total_ms, wl.unit)
+        rec["ms_per_step"] = total_ms / steps
+        rec["gpu_launches"] = steps * wl.launches_per_call
+    else:
+        step_ms = max_over_ranks(sharded["step_ms"], world, device)
+        gather_ms = max_over_ranks(sharded["gather_ms"], world, device)
+        rec["value"] = whole_job_value(world * work, 1, step_ms, wl.unit)
+        rec["ms_per_step"] = step_ms
+        rec["gpu_launches"] = steps * wl.launches_per_call
+        rec["kernel_only"] = {
+            "value": whole_job_value(world * work, 1, per_call_ms, wl.unit),
+            "ms_per_step": per_call_ms,
+            "note": "the shard op alone, graph replays, slowest rank"}
+        rec["gather"] = {
+            "collective": "all_gather_into_tensor per output (NCCL), then the full layout",
+            "ms": gather_ms, "bytes_per_rank": sharded["bytes_per_rank"],
+            "bytes_total": sharded["bytes_total"],
+            "bytes_received_per_rank": sharded["bytes_received_per_rank"],
+            "busbw_GBps": sharded["bytes_received_per_rank"] / (gather_ms * 1e-3) / 1e9}
+        rec["config"]["parallelism"] = (f"{wl.shard_desc} split over {world} ranks (same seed, "
+                                        "sliced) + NCCL all_gather_into_tensor reassembly")
+    rec["clocks"] = sampler.summary()
+
+    # End to end through the public API from pinned host buffers.
+    host_full = tuple(t.cpu() if isinstance(t, torch.Tensor) else t for t in sets[0])
+    del sets
+    torch.cuda.empty_cache()
+    e2e_steps = max(3, min(steps, 10))
+    e = time_e2e(wl, host_full, device, e2e_steps, args.e2e_chunks)
+    e2e_ms = max_over_ranks(e["ms_per_step"], world, device)
+    rec["e2e"] = {"value": whole_job_value(world * work, 1, e2e_ms, wl.unit), "unit": wl.unit,
+                  "h2d_bytes_per_step": e["h2d_bytes_per_step"] * world,
+                  "d2h_bytes_per_step": e["d2h_bytes_per_step"] * world, "ms_per_step": e2e_ms,
+                  "chunks_per_rank": e["chunks"], "api": e["api"]}
+    if with_cpu and world == 1 and wl.cpu_ref is not None and rank == 0:
+        rec["cpu_baseline"] = cpu_baseline(wl, host_full, work, args.cpu_budget)
+    del host_full, probe, op
+    torch.cuda.empty_cache()
+    return rec
+
+
+def _per_op_names(args, world: int, table: dict) -> list[str]:
+    if args.per_op == "none":
+        return []
+    if args.per_op == "all":
+        names = list(table)
+    else:
+        names = [n.strip() for n in args.per_op.split(",") if n.strip()]
+        unknown = [n for n in names if n not in table]
+        if unknown:
+            raise SystemExit(f"unknown --per-op names {unknown}")
+    if world > 1:  # the split BASELINE problems only
+        names = [n for n in names if table[n]().baseline and table[n]().shard is not None]
+    return [n for n in names if n != args.op]
+
+
+def run_ours(args) -> Optional[dict]:
     rank, local_rank, world = dist_env()
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
@@ -702,132 +1089,33 @@ def run_ours(args, wl: Workload) -> Optional[dict]:
 
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=args.pg_timeout),
                                 device_id=device)
-    op = wl.build_op()
-    probe = wl.make_inputs(device, 1235 + rank)
-    set_bytes = sum(t.numel() * t.element_size() for t in probe if isinstance(t, torch.Tensor))
-    out = wl.run(op, probe)
-    outs = out if isinstance(out, (tuple, list)) else (out,)
-    set_bytes += sum(t.numel() * t.element_size() for t in outs)
-    del out, outs
-    n_sets = max(2, min(32, -(-3 * L2_BYTES // max(set_bytes, 1)) + 1))
-    sets = [probe] + [wl.make_inputs(device, 1235 + rank + 1000 * i) for i in range(1, n_sets)]
-    work = wl.work_per_step(op)
-    stream = torch.cuda.current_stream(device)
+    table = workloads()
+    wl = table[args.op]()
+    head = measure(wl, args, rank, local_rank, world, device, not args.no_cpu_baseline, True)
 
-    for i in range(args.warmup):
-        wl.run(op, sets[i % n_sets])
-    torch.cuda.synchronize(device)
-
-    # Graph mode: a CUDA graph holds R consecutive op calls (validation,
-    # output allocation, the library's launches) over the rotating input
-    # sets, each call with outputs of its own; K steps replay it K // R times
-    # (plus a graph of the K % R remaining calls).  Eager mode calls the op
-    # K times from Python.
-    out_bytes = max(1, set_bytes - sum(t.numel() * t.element_size() for t in probe
-                                       if isinstance(t, torch.Tensor)))
-    per_graph = max(1, min(64, (8 << 30) // out_bytes) // n_sets) * n_sets
-    per_graph = min(per_graph, args.steps)
-
-    def capture(n):
-        graph = torch.cuda.CUDAGraph()
-        keep = []
-        with torch.cuda.graph(graph):
-            for i in range(n):
-                keep.append(wl.run(op, sets[i % n_sets]))
-        del keep
-        return graph
-
-    if args.graph:
-        g_main = capture(per_graph)
-        rem = args.steps % per_graph
-        g_rem = capture(rem) if rem else None
-        chunks = [(g_main.replay, per_graph)] * (args.steps // per_graph)
-        if g_rem is not None:
-            chunks.append((g_rem.replay, rem))
-        for _ in range(max(1, -(-args.warmup // per_graph))):
-            g_main.replay()
-        torch.cuda.synchronize(device)
-    else:
-        chunks = [((lambda inp=sets[i % n_sets]: wl.run(op, inp)), 1) for i in range(args.steps)]
-
-    starts = [torch.cuda.Event(enable_timing=True) for _ in chunks]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in chunks]
-    sampler = ClockSampler(local_rank)
-    barrier(world, device)
-    torch.cuda.synchronize(device)
-    with sampler:
-        for i, (fn, _) in enumerate(chunks):
-            starts[i].record(stream)
-            fn()
-            ends[i].record(stream)
-        torch.cuda.synchronize(device)
-    barrier(world, device)
-    total_ms = starts[0].elapsed_time(ends[-1])
-    # Mean step time inside the timed calls (excludes host gaps between them).
-    per_launch_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / args.steps
-    chunk_steps = [n for _, n in chunks]
-    del chunks
-    if args.graph:
-        del g_main, g_rem
-    total_ms = max_over_ranks(total_ms, world, device)
-    per_launch_ms = max_over_ranks(per_launch_ms, world, device)
-
-    # End to end through the public API with pinned host buffers.
-    host_in = [t.cpu().pin_memory() if isinstance(t, torch.Tensor) else t for t in sets[0]]
-    out = wl.run(op, sets[0])
-    outs = out if isinstance(out, (tuple, list)) else (out,)
-    host_out = [torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for o in outs]
-    h2d = sum(t.numel() * t.element_size() for t in host_in if isinstance(t, torch.Tensor))
-    d2h = sum(t.numel() * t.element_size() for t in host_out)
-    e2e_steps = max(3, min(args.steps, 30))
-
-    def e2e_step():
-        dev_in = [t.to(device, non_blocking=True) if isinstance(t, torch.Tensor) else t
-                  for t in host_in]
-        res = wl.run(op, tuple(dev_in))
-        res = res if isinstance(res, (tuple, list)) else (res,)
-        for h, d in zip(host_out, res):
-            h.copy_(d, non_blocking=True)
-
-    for _ in range(2):
-        e2e_step()
-    torch.cuda.synchronize(device)
-    barrier(world, device)
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(e2e_steps):
-        e2e_step()
-    e1.record(stream)
-    torch.cuda.synchronize(device)
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps, world, device)
-    barrier(world, device)
-
-    gather = None
-    if args.gather and world > 1:
-        res = wl.run(op, sets[0])
-        res = res if isinstance(res, (tuple, list)) else (res,)
-        gather, fulls = gather_outputs(res, world, device)
-        gather["op_plus_gather_ms"] = per_launch_ms + gather["ms"]
-        del res, fulls
+    weak = None
+    if world > 1 and not args.no_weak:
+        # Secondary figure: every rank runs the whole problem (replicas).
+        full = wl.make_inputs(device, SEED + rank)
+        op = wl.build_op(full)
+        n_sets = max(2, min(32, -(-3 * L2_BYTES // max(_nbytes(full) * 2, 1)) + 1))
+        sets = [full] + [wl.make_inputs(device, SEED + rank + 1000 * i) for i in range(1, n_sets)]
         barrier(world, device)
+        k = time_calls(wl, op, sets, min(args.steps, args.per_op_steps), args.warmup, args.graph,
+                       device, torch.cuda.current_stream(device))
+        barrier(world, device)
+        ms = max_over_ranks(k["per_call_ms"], world, device)
+        weak = {"value": whole_job_value(world * wl.work(op), 1, ms, wl.unit),
+                "ms_per_step": ms, "note": "every rank runs the whole problem (replicas)"}
+        del sets, full, op
+        torch.cuda.empty_cache()
 
-    scale = 1e9 if wl.unit == "GB/s" else 1e12
-    value = whole_job_value(work, args.steps, total_ms, world, wl.unit)
-    roof_unit = wl.roof_unit or wl.unit
-    roof_work = wl.roof_work_per_step(op) if wl.roof_work_per_step else work
-    roof_scale = 1e9 if roof_unit == "GB/s" else 1e12
-    achieved = roof_work / (per_launch_ms * 1e-3) / roof_scale
-    peaks, peak_kind = load_peaks()
-    if roof_unit == "GB/s":
-        peak = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
-        peak_unit = "GB/s"
-    else:
-        peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
-        peak_unit = "TFLOP/s"
-    clocks = sampler.summary()
+    per_op = {}
+    for name in _per_op_names(args, world, table):
+        per_op[name] = measure(table[name](), args, rank, local_rank, world, device,
+                               not args.no_cpu_baseline, False)
     if world > 1:
         import torch.distributed as dist
 
@@ -835,92 +1123,131 @@ def run_ours(args, wl: Workload) -> Optional[dict]:
     if rank != 0:
         return None
     line = {
-        "metric": wl.metric, "value": value, "unit": wl.unit, "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype,
+        "metric": wl.metric, "value": head["value"], "unit": wl.unit, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": head["ms_per_step"],
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": wl.dtype,
         "data": "synthetic (seeded torch.randn of the BASELINE shapes)",
-        "config": {**wl.config, "parallelism": f"independent batch per GPU x{world}",
-                   "l2": f"rotating {n_sets} input/output sets "
-                         f"({n_sets * set_bytes / 2**20:.0f} MiB) > 126 MB L2",
-                   "timing": (f"CUDA-graph replays of {chunk_steps[0]} op calls each, "
-                              "CUDA events around each replay" if args.graph else
-                              "eager op calls, CUDA events per step")},
-        "roofline": {"bound": wl.bound, "achieved": achieved, "peak": peak, "unit": peak_unit,
-                     "frac": achieved / peak, "traffic": load_traffic(wl.name),
-                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json)" if peak_kind ==
-                     "measured" else "fallback", "per_launch_ms": per_launch_ms,
-                     "algorithmic_per_launch": roof_work},
-        "e2e": {"value": whole_job_value(work, 1, e2e_ms, world, wl.unit), "unit": wl.unit,
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
-                "api": f"{type(op).__name__}.__call__ with pinned host buffers"},
-        "gpu_launches": args.steps * wl.launches_per_step,
-        "clocks": clocks,
+        "config": {**head["config"], "l2": head["l2"], "timing": head["timing"]},
+        "roofline": head["roofline"], "e2e": head["e2e"],
+        "gpu_launches": head["gpu_launches"], "clocks": head["clocks"],
     }
-    if gather is not None:
-        line["gather"] = gather
-    if world == 1 and not args.no_cpu_baseline and wl.cpu_fn is not None:
-        line["cpu_baseline"] = time_cpu_baseline(wl)
+    line["config"].setdefault("parallelism", "dp1 (one GPU, the whole problem)")
+    for key in ("kernel_only", "gather", "cpu_baseline"):
+        if key in head:
+            line[key] = head[key]
+    if weak is not None:
+        line["weak"] = weak
+    line["per_op"] = {wl.name: _compact(head), **{n: _compact(r) for n, r in per_op.items()}}
     return line
 
 
+def _compact(rec: dict) -> dict:
+    out = {"value": rec["value"], "unit": rec["unit"], "ms_per_step": rec["ms_per_step"],
+           "workload": rec["config"]["workload"],
+           "roofline": {k: rec["roofline"][k] for k in ("bound", "achieved", "peak", "unit",
+                                                         "frac", "traffic", "per_launch_ms")},
+           "e2e": {k: rec["e2e"][k] for k in ("value", "ms_per_step", "h2d_bytes_per_step",
+                                               "d2h_bytes_per_step", "chunks_per_rank")},
+           "clocks": rec["clocks"], "gpu_launches": rec["gpu_launches"]}
+    for key in ("kernel_only", "gather", "cpu_baseline"):
+        if key in rec:
+            out[key] = rec[key]
+    return out
+
+
 # ----------------------------------------------------------- reference arm
-def run_reference(args, wl: Workload) -> Optional[dict]:
+def run_reference(args) -> Optional[dict]:
+    """The reference's CPU program (its tests' torch ref_program, restated in
+    oracle/) on the host cores, rank 0 only: K timed calls after W warm-up
+    calls on the headline op's full configuration, and at N = 1 every other
+    op's CPU baseline under ``per_op``."""
     rank, _, world = dist_env()
     if rank != 0:
         return None
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    full = wl.make_inputs(torch.device("cpu"), 1235)
-    rows = args.ref_rows
-    sample = wl.cpu_slice(full, rows)
+    table = workloads()
+    wl = table[args.op]()
+    cpu = torch.device("cpu")
+    full = wl.make_inputs(cpu, SEED)
+    inputs = wl.cpu_sample(full) if wl.cpu_sample else full
+    units = host_work(wl, inputs)
     for _ in range(args.warmup):
-        wl.cpu_fn(sample)
+        wl.cpu_ref(inputs)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        wl.cpu_fn(sample)
+        wl.cpu_ref(inputs)
     sec = (time.perf_counter() - t0) / args.steps
     scale = 1e9 if wl.unit == "GB/s" else 1e12
-    value = wl.cpu_units(sample) / sec / scale
-    desc = ", ".join(f"{tuple(t.shape)}" for t in sample if isinstance(t, torch.Tensor))
-    return {
+    value = units / sec / scale
+    desc = (f"sample: {wl.cpu_sample_desc}" if wl.cpu_sample else "the full configuration")
+    line = {
         "impl": "reference", "metric": wl.metric, "value": value, "unit": wl.unit,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": wl.dtype,
         "data": "synthetic (seeded torch.randn of the BASELINE shapes)",
         "config": {**wl.config, "parallelism": "host CPU, rank 0 only"},
         "cpu_baseline": {"value": value, "unit": wl.unit, "cores": torch.get_num_threads(),
-                         "kind": "port",
-                         "sample": f"reference torch CPU ref program (restated in oracle/) on "
-                                   f"inputs {desc} per step"},
+                         "kind": "port", "same_config": wl.cpu_sample is None,
+                         "sample": f"reference torch CPU program (restated in oracle/) on "
+                                   f"{desc}, every step"},
         "e2e": {"value": value, "unit": wl.unit, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
+    del full, inputs
+    if world == 1 and args.per_op not in (None, "none"):
+        per_op = {}
+        names = list(table) if args.per_op == "all" else [
+            n.strip() for n in args.per_op.split(",") if n.strip()]
+        for name in names:
+            if name == args.op:
+                continue
+            w = table[name]()
+            if w.cpu_ref is None:
+                continue
+            f = w.make_inputs(cpu, SEED)
+            per_op[name] = cpu_baseline(w, f, host_work(w, f), args.cpu_budget)
+            del f
+        line["per_op"] = per_op
+    return line
 
 
 def main() -> None:
     ap = argparse.ArgumentParser(description="B200 TileOPs hot-path benchmark")
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--op", default="fused_add_layer_norm")
-    ap.add_argument("--ref-rows", type=int, default=256,
-                    help="rows of the batch the CPU reference processes per step")
+    ap.add_argument("--op", default="fused_add_layer_norm", help="the headline op")
+    ap.add_argument("--per-op", default=None,
+                    help="'all', 'none' or a comma list of ops measured beside the headline "
+                         "(N > 1: the BASELINE ops among them).  Default: 'all' for our arm, "
+                         "'none' for the reference arm (our line carries every op's CPU "
+                         "baseline already)")
+    ap.add_argument("--per-op-steps", type=int, default=20,
+                    help="timed calls per op in per_op (the headline uses --steps)")
+    ap.add_argument("--e2e-chunks", type=int, default=16,
+                    help="chunks per step in the end-to-end leg (at most)")
+    ap.add_argument("--cpu-budget", type=float, default=10.0,
+                    help="seconds of CPU time per op for the CPU baseline")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-weak", action="store_true",
+                    help="N > 1: skip the per-rank replica (weak scaling) figure")
+    ap.add_argument("--pg-timeout", type=int, default=300,
+                    help="process-group timeout in seconds (a rank that left ends the "
+                         "others' next collective with an error after this long)")
     ap.add_argument("--no-graph", dest="graph", action="store_false",
                     help="time eager op calls instead of CUDA-graph replays")
-    ap.add_argument("--gather", action="store_true",
-                    help="N > 1: also time reassembling every rank's outputs on every rank "
-                         "(all_gather_into_tensor; reported under 'gather', not in 'value')")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
+    if args.per_op is None:
+        args.per_op = "all" if args.impl == "ours" else "none"
     table = workloads()
     if args.op not in table:
         raise SystemExit(f"unknown --op {args.op}; choose from {sorted(table)}")
-    wl = table[args.op]()
-    line = run_reference(args, wl) if args.impl == "reference" else run_ours(args, wl)
+    line = run_reference(args) if args.impl == "reference" else run_ours(args)
     if line is not None:
         print(json.dumps(line), flush=True)
 

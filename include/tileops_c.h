@@ -59,6 +59,18 @@ const char* tileops_status_string(int status);
  * tileops_gdn_prefill_varlen_fwd.  The first code set is kept until cleared. */
 int tileops_device_error_flag(void* stream, int clear);
 
+/* Self-test of the bounded-wait give-up path shared by the tensor-core
+ * kernels: one warp allocates 32 TMEM columns, starts a bulk copy of `bytes`
+ * (16..4096, a multiple of 16) from `src` (16-byte aligned device memory),
+ * waits on an mbarrier nothing arrives on for `limit_ns` (1e3..1e9) and then,
+ * as every kernel here does on a timeout, sets device error 1, waits for its
+ * copy to land, frees TMEM and returns.  `out` (4 device ints) receives:
+ * [0] 1 if the wait gave up, [1] 1 if the copy landed, [2] the sum of the
+ * copied bytes, [3] 1 once TMEM was freed.  A diagnostic of this library with
+ * no counterpart in the reference (its kernels have no bounded waits). */
+int tileops_selftest_wait_timeout(const void* src, int64_t bytes, int64_t limit_ns, int* out,
+                                  void* stream);
+
 /* ---- elementwise unary (flat, n elements; y may not alias x) ----------- */
 
 /* y = x * clamp(x + 3, 0, 6) / 6 in fp32, rounded once.  dtype f32/f16/bf16.
@@ -271,7 +283,9 @@ int tileops_gdn_prefill_varlen_fwd(const void* q, const void* k, const void* v, 
  * chunks of 64 tokens summed over batch * heads at dk = dv = 128) return
  * TILEOPS_EBADSHAPE before anything is enqueued.  All calls share the array,
  * so calls whose kernels overlap on the GPU race.  The first call on a device
- * looks up the array's device address; make it outside any stream capture.
+ * looks up the device addresses of the array and of the device error word
+ * (cudaGetSymbolAddress, which may load the module); make that first call
+ * outside any stream capture.
  * This entry point has no counterpart in the reference. */
 int tileops_gdn_prefill_fwd_noalloc(const void* q, const void* k, const void* v, const float* g,
                                     const float* beta, const float* initial_state, void* o,

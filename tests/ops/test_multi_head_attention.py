@@ -48,8 +48,13 @@ PARAMS = [
     pytest.param(1, 1024, 8, 64, False, torch.bfloat16, marks=pytest.mark.smoke),
     pytest.param(1, 1024, 8, 64, True, torch.bfloat16, marks=pytest.mark.smoke),
     pytest.param(2, 512, 4, 128, True, torch.float16, marks=pytest.mark.smoke),
-    pytest.param(4, 2048, 4, 128, False, torch.float16, marks=pytest.mark.full),
-    pytest.param(2, 4096, 4, 128, False, torch.bfloat16, marks=pytest.mark.full),
+    # The reference's two "full" cases at their own sizes
+    # (TO/tests/ops/test_multi_head_attention.py:74-93), every output element
+    # compared with CPU SDPA in the input dtype.
+    pytest.param(16, 2048, 16, 128, False, torch.float16, marks=pytest.mark.full,
+                 id="full-fwd-fp16"),
+    pytest.param(4, 4096, 16, 128, False, torch.bfloat16, marks=pytest.mark.full,
+                 id="full-fwd-bf16"),
     pytest.param(2, 2048, 8, 128, True, torch.bfloat16, marks=pytest.mark.full),
 ]
 

@@ -33,7 +33,7 @@ def test_every_traffic_entry_names_a_committed_profile():
 def test_default_workload_has_traffic_and_a_cpu_baseline():
     wl = bench.workloads()["fused_add_layer_norm"]()
     assert bench.load_traffic(wl.name) is not None
-    assert wl.cpu_fn is not None and wl.unit == "GB/s" and wl.bound == "hbm"
+    assert wl.cpu_ref is not None and wl.unit == "GB/s" and wl.bound == "hbm"
 
 
 def test_clock_summary_drops_idle_samples_and_decodes_reasons():

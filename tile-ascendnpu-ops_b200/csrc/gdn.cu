@@ -1500,9 +1500,13 @@ extern "C" int tileops_gdn_prefill_varlen_fwd(const void* q, const void* k, cons
 //    (different streams, or different host threads) race on it.
 //  * Nothing in the scratch has to start at zero: the prepare kernel writes
 //    every byte the scan kernel reads for the chunks in use.
-//  * The device address of the array is looked up (cudaGetSymbolAddress) on
-//    the first call on each device, with that device current; make that first
-//    call outside any stream capture.
+//  * The first call on each device (with that device current) looks up the
+//    device addresses of both library symbols a GDN call uses -- this array
+//    and the device error word that the kernels' bounded waits write -- with
+//    cudaGetSymbolAddress, which may load the module lazily; make that first
+//    call outside any stream capture.  Later calls only read the cached
+//    addresses.  Devices are cached by index up to 63; a higher device index
+//    is refused with TILEOPS_ELAUNCH.
 constexpr size_t kGdnStaticScratchBytes = static_cast<size_t>(16) << 20;
 static __device__ __align__(256) unsigned char g_gdn_static_scratch[kGdnStaticScratchBytes];
 
@@ -1514,6 +1518,8 @@ void* gdn_static_scratch_ptr() {
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
   std::lock_guard<std::mutex> lock(mu);
   if (!cached[dev]) {
+    // Resolve the error word too, so one first call covers every lookup.
+    if (!tileops::device_error_ptr()) return nullptr;
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_gdn_static_scratch) != cudaSuccess) return nullptr;
     cached[dev] = p;

@@ -84,6 +84,7 @@ _SIGNATURES: dict[str, list] = {
     "tileops_gla_decode_fwd": [_p] * 7 + [_i64] * 4 + [_d, _i, _p],
     "tileops_ssd_chunk_scan_fwd": [_p] * 7 + [_i64] * 7 + [_i, _p],
     "tileops_device_error_flag": [_p, _i],
+    "tileops_selftest_wait_timeout": [_p, _i64, _i64, _p, _p],
     "tileops_abi_version": [],
     "tileops_status_string": [_i],
 }

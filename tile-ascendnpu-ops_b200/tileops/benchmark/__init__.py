@@ -1,3 +1,11 @@
-from tileops.benchmark.benchmark_base import BenchmarkReport, bench_kernel, roofline_report
+from tileops.benchmark.benchmark_base import (
+    BenchmarkBase,
+    BenchmarkReport,
+    ManifestBenchmark,
+    bench_kernel,
+    roofline_report,
+    workloads_to_params,
+)
 
-__all__ = ["BenchmarkReport", "bench_kernel", "roofline_report"]
+__all__ = ["BenchmarkBase", "BenchmarkReport", "ManifestBenchmark", "bench_kernel",
+           "roofline_report", "workloads_to_params"]
