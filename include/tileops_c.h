@@ -59,15 +59,18 @@ const char* tileops_status_string(int status);
  * tileops_gdn_prefill_varlen_fwd.  The first code set is kept until cleared. */
 int tileops_device_error_flag(void* stream, int clear);
 
-/* Self-test of the bounded-wait give-up path shared by the tensor-core
- * kernels: one warp allocates 32 TMEM columns, starts a bulk copy of `bytes`
+/* Self-test of the give-up path the tensor-core kernels take when a wait
+ * runs out: one warp allocates 32 TMEM columns, starts a bulk copy of `bytes`
  * (16..4096, a multiple of 16) from `src` (16-byte aligned device memory),
- * waits on an mbarrier nothing arrives on for `limit_ns` (1e3..1e9) and then,
- * as every kernel here does on a timeout, sets device error 1, waits for its
- * copy to land, frees TMEM and returns.  `out` (4 device ints) receives:
+ * waits (polling, so the wait always ends) on an mbarrier nothing arrives on
+ * for `limit_ns` (1e3..1e9) and then, as every kernel here does on a
+ * timeout, sets device error 1, waits for its
+ * copy to land, frees TMEM and returns.  `out` (6 device ints) receives:
  * [0] 1 if the wait gave up, [1] 1 if the copy landed, [2] the sum of the
- * copied bytes, [3] 1 once TMEM was freed.  A diagnostic of this library with
- * no counterpart in the reference (its kernels have no bounded waits). */
+ * copied bytes, [3] 1 once TMEM was freed, [4] / [5] the low / high 32 bits
+ * of the nanoseconds the wait took before giving up.  A diagnostic of this
+ * library with no counterpart in the reference (its kernels have no bounded
+ * waits). */
 int tileops_selftest_wait_timeout(const void* src, int64_t bytes, int64_t limit_ns, int* out,
                                   void* stream);
 

@@ -4,8 +4,9 @@ The reference has no test for this op; its only pin is the probe's
 sequential golden (examples/gdn_prefill/probe/gdn_prefill_probe.py:60-77),
 restated in the oracle and checked bit-for-bit against fixtures of it.  The
 kernel runs the chunked WY form with bf16 tensor-core operands and an fp32
-state; outputs are compared against the fp32 golden with the north-star
-16-bit tolerance (atol = rtol = 1e-2) for o and for the fp32 final state.
+state; o is compared against the fp32 golden with the north-star 16-bit
+tolerance (atol = rtol = 1e-2), the fp32 final state with the bound measured
+against an fp64 recurrence (STATE_TOL below).
 Covered: the probe's own cases at the supported head dims, BASELINE
 distributions at small sizes, ragged lengths (T not a multiple of 64),
 initial-state chaining (two halves == one run), dk = dv = 64, and the
@@ -22,7 +23,14 @@ from tileops.workloads.linear_attention import GdnPrefillWorkload
 
 pytestmark = pytest.mark.gpu
 
-TOL = dict(atol=1e-2, rtol=1e-2)
+TOL = dict(atol=1e-2, rtol=1e-2)  # the bf16 output o: the north-star 16-bit tolerance
+# The fp32 final state: the state enters the tensor cores in bf16 each chunk
+# (S as the B operand of Wk S and Q S; err and the decayed err in bf16), so
+# fp32's 1e-5 is out of reach.  Measured against an fp64 recurrence on the
+# BASELINE distributions (B=4, T=8192, H=16, and every shape of this file):
+# max |error| 2.4e-3 to 4.7e-3 at |S| <= 0.93, within atol 3.8e-3 + rtol 1e-3;
+# the bound keeps a 2x margin.
+STATE_TOL = dict(atol=8e-3, rtol=1e-3)
 
 
 def _run(q, k, v, g, beta, h0=None):
@@ -35,7 +43,7 @@ def _check(q, k, v, g, beta, h0=None):
     o, s = _run(q, k, v, g, beta, h0)
     o_ref, s_ref = ref.gdn_prefill_bthd(q, k, v, g, beta, None, h0)
     torch.testing.assert_close(o.cpu().float(), o_ref.float(), **TOL)
-    torch.testing.assert_close(s.cpu(), s_ref, **TOL)
+    torch.testing.assert_close(s.cpu(), s_ref, **STATE_TOL)
     return o, s
 
 
@@ -108,7 +116,7 @@ def test_baseline_config_sampled_heads():
         sl = (slice(bi, bi + 1), slice(None), slice(hi, hi + 1))
         o_ref, s_ref = ref.gdn_prefill_bthd(q[sl], k[sl], v[sl], g[sl], beta[sl])
         torch.testing.assert_close(o[sl].cpu().float(), o_ref.float(), **TOL)
-        torch.testing.assert_close(s[bi : bi + 1, hi : hi + 1].cpu(), s_ref, **TOL)
+        torch.testing.assert_close(s[bi : bi + 1, hi : hi + 1].cpu(), s_ref, **STATE_TOL)
 
 
 def test_misaligned_final_state_runs_the_register_scan():
@@ -131,7 +139,7 @@ def test_misaligned_final_state_runs_the_register_scan():
     torch.cuda.synchronize()
     o_ref, s_ref = ref.gdn_prefill_bthd(q, k, v, g, beta)
     torch.testing.assert_close(o.cpu().float(), o_ref.float(), **TOL)
-    torch.testing.assert_close(hT.view(B, H, DK, DV).cpu(), s_ref, **TOL)
+    torch.testing.assert_close(hT.view(B, H, DK, DV).cpu(), s_ref, **STATE_TOL)
     o_tc, s_tc = _run(q, k, v, g, beta)
     torch.testing.assert_close(o.float(), o_tc.float(), atol=2e-2, rtol=2e-2)
 

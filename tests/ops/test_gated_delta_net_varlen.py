@@ -21,7 +21,14 @@ from tileops.workloads.linear_attention import GdnPrefillWorkload
 
 pytestmark = pytest.mark.gpu
 
-TOL = dict(atol=1e-2, rtol=1e-2)
+TOL = dict(atol=1e-2, rtol=1e-2)  # the bf16 output o: the north-star 16-bit tolerance
+# The fp32 final state: the state enters the tensor cores in bf16 each chunk
+# (S as the B operand of Wk S and Q S; err and the decayed err in bf16), so
+# fp32's 1e-5 is out of reach.  Measured against an fp64 recurrence on the
+# BASELINE distributions (B=4, T=8192, H=16, and every shape of this file):
+# max |error| 2.4e-3 to 4.7e-3 at |S| <= 0.93, within atol 3.8e-3 + rtol 1e-3;
+# the bound keeps a 2x margin.
+STATE_TOL = dict(atol=8e-3, rtol=1e-3)
 
 
 def _cu(lengths):
@@ -62,7 +69,7 @@ def test_matches_golden(lengths, dk, dv):
     o, s = _run_varlen(q, k, v, g, beta, cu, h0)
     o_ref, s_ref = ref.gdn_prefill_varlen(q, k, v, g, beta, cu, None, h0)
     torch.testing.assert_close(o.cpu().float(), o_ref.float(), **TOL)
-    torch.testing.assert_close(s.cpu(), s_ref, **TOL)
+    torch.testing.assert_close(s.cpu(), s_ref, **STATE_TOL)
 
 
 @pytest.mark.parametrize("dk", [128, 64])
@@ -170,7 +177,7 @@ def test_fused_qk_l2norm_uniform(dk, dv):
     o, s = op(q, k, v, g, beta, h0, use_qk_l2norm_in_kernel=True)
     o_ref, s_ref = ref.gdn_prefill_bthd(q, k, v, g, beta, None, h0, qk_l2norm=True)
     torch.testing.assert_close(o.cpu().float(), o_ref.float(), **TOL)
-    torch.testing.assert_close(s.cpu(), s_ref, **TOL)
+    torch.testing.assert_close(s.cpu(), s_ref, **STATE_TOL)
 
 
 def test_fused_qk_l2norm_varlen():
@@ -183,7 +190,7 @@ def test_fused_qk_l2norm_varlen():
         q, k, v, g, beta, h0, cu_seqlens=cu, use_qk_l2norm_in_kernel=True)
     o_ref, s_ref = ref.gdn_prefill_varlen(q, k, v, g, beta, cu, None, h0, qk_l2norm=True)
     torch.testing.assert_close(o.cpu().float(), o_ref.float(), **TOL)
-    torch.testing.assert_close(s.cpu(), s_ref, **TOL)
+    torch.testing.assert_close(s.cpu(), s_ref, **STATE_TOL)
 
 
 def test_fla_style_functional_form():

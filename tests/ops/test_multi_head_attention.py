@@ -23,7 +23,12 @@ from tileops.workloads.attention import MhaFwdWorkload
 
 pytestmark = pytest.mark.gpu
 
-LSE_TOL = dict(atol=2e-3, rtol=1e-4)
+# The fp32 log2-domain LSE.  Measured against an fp64 logsumexp of the same
+# bf16 / fp16 q, k (BASELINE (8, 4096, 32, 128) both masks, the reference's
+# (16, 2048, 16, 128) fp16, every ragged length here): max |error| 1.5e-6,
+# max relative error 8.1e-6 (|lse| < 1 for one-key rows); the fp32 oracle
+# adds about 1e-6.  The bound keeps a 4x margin.
+LSE_TOL = dict(atol=1e-5, rtol=1e-6)
 
 
 def out_tol(dtype):

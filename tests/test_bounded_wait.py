@@ -1,13 +1,13 @@
 """A bounded device-side wait that runs out, on the GPU, without faulting it.
 
 Every tensor-core kernel of the library (attention, GDN, SSD chunk scan,
-dense conv1d) bounds its mbarrier waits; on a timeout it records device
-error 1, lets its own copies land, frees TMEM and returns, so the context
-stays usable.  ``tileops_selftest_wait_timeout`` runs that give-up path on
-purpose: it waits ~1 ms on an mbarrier nothing arrives on while holding TMEM
-and a bulk copy in flight.  The test checks what the host sees afterwards:
-the status word, the drained copy, that the flag clears, and that a normal op
-launched next runs clean.
+dense conv1d) has the same give-up path: when a wait runs out it records
+device error 1, lets its own copies land, frees TMEM and returns, so the
+context stays usable.  ``tileops_selftest_wait_timeout`` runs that path on
+purpose: it waits ~1 ms, polling, on an mbarrier nothing arrives on while
+holding TMEM and a bulk copy in flight.  The test checks what the host sees
+afterwards: the status word, the drained copy, the time the wait took, that
+the flag clears, and that a tensor-core op launched next runs clean.
 """
 
 import ctypes
@@ -24,7 +24,7 @@ pytestmark = pytest.mark.gpu
 def _run_selftest(nbytes: int, limit_ns: int):
     dev = torch.device("cuda", 0)
     src = (torch.arange(nbytes, device=dev) % 251).to(torch.uint8)
-    out = torch.zeros(4, dtype=torch.int32, device=dev)
+    out = torch.zeros(6, dtype=torch.int32, device=dev)
     stream = _native.stream_handle(dev)
     status = _native.lib().tileops_selftest_wait_timeout(
         ctypes.c_void_p(src.data_ptr()), nbytes, limit_ns, ctypes.c_void_p(out.data_ptr()), stream)
@@ -42,12 +42,17 @@ def test_wait_runs_out_reports_and_recovers():
     assert got[1] == 1, "the drain did not see the in-flight copy land"
     assert got[2] == int(src.to(torch.int64).sum()), "copied bytes read before they landed"
     assert got[3] == 1, "TMEM was not released"
+    waited_ns = (got[5] << 32) | (got[4] & 0xffffffff)
+    # It gave up once the limit had passed, and not much later: the polls are
+    # 64 ns apart and the timer is read after each one.
+    assert 1_000_000 <= waited_ns < 50_000_000, waited_ns
     # The host sees the timeout code once, and reading with clear resets it.
     assert _native.lib().tileops_device_error_flag(stream, 1) == 1
     assert _native.lib().tileops_device_error_flag(stream, 0) == 0
     # The context is still usable: a real tensor-core op runs and sets no flag.
-    q = torch.randn(1, 256, 2, 128, device="cuda", dtype=torch.bfloat16)
-    o, lse = MultiHeadAttentionFwdOp(1, 2, 256, 128, False, torch.bfloat16)(q, q, q)
+    q, k, v = (torch.randn(1, 256, 2, 128, device="cuda", dtype=torch.bfloat16)
+               for _ in range(3))
+    o, lse = MultiHeadAttentionFwdOp(1, 2, 256, 128, False, torch.bfloat16)(q, k, v)
     torch.cuda.synchronize()
     assert torch.isfinite(o.float()).all() and torch.isfinite(lse).all()
     assert _native.lib().tileops_device_error_flag(stream, 1) == 0
@@ -66,7 +71,7 @@ def test_two_timeouts_in_a_row():
 def test_selftest_rejects_bad_arguments():
     dev = torch.device("cuda", 0)
     src = torch.zeros(8192, dtype=torch.uint8, device=dev)
-    out = torch.zeros(4, dtype=torch.int32, device=dev)
+    out = torch.zeros(6, dtype=torch.int32, device=dev)
     stream = _native.stream_handle(dev)
     f = _native.lib().tileops_selftest_wait_timeout
     p, o = ctypes.c_void_p(src.data_ptr()), ctypes.c_void_p(out.data_ptr())

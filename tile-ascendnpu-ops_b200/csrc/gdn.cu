@@ -921,9 +921,11 @@ __global__ void __launch_bounds__(256, 1)
 //   MMA2  D2 = [U ; QKm] Es         (rows 64-127: QKm err)
 //   math  S -> Sb (bf16), S *= e^(gc_last of chunk c+1)   -> next chunk
 //   math  o = scale e^gc (Q S) + QKm err   (rows 64-127, off the chain)
-// The chain from one chunk to the next is MMA1, the err pass, MMA3 and the
-// state pass; D1 is triple- and D2 double-buffered so the output pass of
-// chunk c overlaps chunk c+1.
+// The chain from one chunk to the next is MMA1, the err pass (Ed only: Es
+// follows on its own barrier for MMA2), MMA3 and the state pass (up to the
+// bf16 copy Sb: the pre-scaled TMEM copy is written after s_ready, since only
+// MMA3 of the next chunk, which waits for e_ready, reads it); D1 is triple-
+// and D2 double-buffered so the output pass of chunk c overlaps chunk c+1.
 // Shared memory per stage (128-byte swizzled tiles, 64 KB): A1 = [-Wk ; Q]
 // as two chunks of [128][64]; K [64][128]; [U ; QKm] as one [128][64] tile
 // (the B operand of MMA0 is its U half; as the A operand of MMA2 its U rows
@@ -952,7 +954,7 @@ struct ScanTcSmem {
 
 struct ScanTcBars {
   uint64_t full[kTcStages], empty[kTcStages];
-  uint64_t s_ready, d1_full, e_ready, d3_full, d2_full, drain;
+  uint64_t s_ready, d1_full, e_ready, es_ready, d3_full, d2_full, drain;
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -1005,6 +1007,7 @@ __global__ void __launch_bounds__(kScanTcThreads, 1)
     mbar_init(&bars->s_ready, kScanTcMath);
     mbar_init(&bars->d1_full, 1);
     mbar_init(&bars->e_ready, kScanTcMath);
+    mbar_init(&bars->es_ready, kScanTcMath / 2);
     mbar_init(&bars->d3_full, 1);
     mbar_init(&bars->d2_full, 1);
     mbar_init(&bars->drain, 1);
@@ -1110,6 +1113,8 @@ __global__ void __launch_bounds__(kScanTcThreads, 1)
           mma_f16_ss(t_s, desc_advance(st_mn, so + L::kK + kk * 2048),
                      desc_advance(ed_d, kk * 2048), id_mnmn, 1);
         mma_commit(&bars->d3_full);
+        if (!mbar_wait(&bars->es_ready, c & 1, err, abort_flag)) break;
+        tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kC / 16; ++kk)  // D2 = [U ; QKm] Es
           mma_f16_ss(t_d2(c), desc_advance(st_k, so + L::kUQ + kk * 32),
@@ -1134,8 +1139,8 @@ __global__ void __launch_bounds__(kScanTcThreads, 1)
     uint8_t* Ed = sm + L::kEd;
     bool ok = true;
     // This thread's 32 state values (fp32, row r, columns cb..cb+31) -> Sb in
-    // bf16; then, scaled by e^gc_last of chunk `next`, back to TMEM.
-    auto publish = [&](uint32_t (&x)[32], int next) {
+    // bf16, then s_ready: MMA1 of the next chunk needs only Sb.
+    auto publish_sb = [&](const uint32_t (&x)[32]) {
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         uint4 pk;
@@ -1146,6 +1151,13 @@ __global__ void __launch_bounds__(kScanTcThreads, 1)
         *reinterpret_cast<uint4*>(Sb + swz(r, cb + 8 * u)) = pk;
       }
       fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&bars->s_ready);
+    };
+    // Then, off the chain, the same values scaled by e^gc_last of chunk `next`
+    // back to TMEM: MMA3 of chunk `next` accumulates onto them, and the issuer
+    // starts it only after this thread's next e_ready arrival.
+    auto prescale = [&](uint32_t (&x)[32], int next) {
       const int s = next % kTcStages;
       if (!mbar_wait(&bars->full[s], (next / kTcStages) & 1, err, abort_flag)) {
         ok = false;
@@ -1163,9 +1175,8 @@ __global__ void __launch_bounds__(kScanTcThreads, 1)
       for (int i = 0; i < 32; ++i)
         x[i] = __float_as_uint(
             h0 ? h0[((static_cast<int64_t>(b) * H + h) * DK + r) * DV + v0 + cb + i] : 0.0f);
-      publish(x, 0);
-      tc_fence_before();
-      mbar_arrive(&bars->s_ready);
+      publish_sb(x);
+      prescale(x, 0);
     }
     for (int c = 0; ok && c < nchunks; ++c) {
       const int s = c % kTcStages;
@@ -1182,35 +1193,48 @@ __global__ void __launch_bounds__(kScanTcThreads, 1)
         tmem_ld32(t_d1(c) + lane_off + cb, x);
         tmem_wait_ld_regs(x);
         const float dec = tail[kC + l];
+        // Ed (the decayed err, for MMA3 on the chain) first, then Es (MMA2).
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          uint4 pe, pd;
-          uint32_t* pew = reinterpret_cast<uint32_t*>(&pe);
+          uint4 pd;
           uint32_t* pdw = reinterpret_cast<uint32_t*>(&pd);
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float e0 = __uint_as_float(x[8 * u + 2 * e]);
-            const float e1 = __uint_as_float(x[8 * u + 2 * e + 1]);
-            pew[e] = pack_bf16(e0, e1);
-            pdw[e] = pack_bf16(dec * e0, dec * e1);
-          }
-          *reinterpret_cast<uint4*>(Es + swz(l, cb + 8 * u)) = pe;
+          for (int e = 0; e < 4; ++e)
+            pdw[e] = pack_bf16(dec * __uint_as_float(x[8 * u + 2 * e]),
+                               dec * __uint_as_float(x[8 * u + 2 * e + 1]));
           *reinterpret_cast<uint4*>(Ed + swz(l, cb + 8 * u)) = pd;
         }
         if (l >= zpad) {
           // A padding row of packed sequences: its K row (box cb / 32 of the K tile) -> 0 before
-          // MMA3 reads it (this thread waited for the stage in `publish`).
+          // MMA3 reads it (this thread waited for the stage in `prescale`).
           uint4* krow = reinterpret_cast<uint4*>(sm + s * L::kStage + L::kK + (cb >> 5) * 8192 +
                                                  l * 128);
 #pragma unroll
           for (int u = 0; u < 8; ++u) krow[u] = make_uint4(0u, 0u, 0u, 0u);
         }
         fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(&bars->e_ready);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          uint4 pe;
+          uint32_t* pew = reinterpret_cast<uint32_t*>(&pe);
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            pew[e] = pack_bf16(__uint_as_float(x[8 * u + 2 * e]),
+                               __uint_as_float(x[8 * u + 2 * e + 1]));
+          *reinterpret_cast<uint4*>(Es + swz(l, cb + 8 * u)) = pe;
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&bars->es_ready);
       } else {
-        qsc = tail[l];  // read before e_ready: the stage is refilled after MMA2
+        // Read before e_ready: the stage is refilled after MMA2, which the
+        // issuer starts only after e_ready.  This arrival also orders this
+        // thread's TMEM store of the pre-scaled state before MMA3.
+        qsc = tail[l];
+        tc_fence_before();
+        mbar_arrive(&bars->e_ready);
       }
-      tc_fence_before();
-      mbar_arrive(&bars->e_ready);
       // The new state: to Sb (bf16) and, pre-scaled for the next chunk, to TMEM.
       if (!mbar_wait(&bars->d3_full, c & 1, err, abort_flag)) { ok = false; break; }
       tc_fence_after();
@@ -1219,9 +1243,8 @@ __global__ void __launch_bounds__(kScanTcThreads, 1)
         tmem_ld32(t_s + lane_off + cb, x);
         tmem_wait_ld_regs(x);
         if (c + 1 < nchunks) {
-          publish(x, c + 1);
-          tc_fence_before();
-          mbar_arrive(&bars->s_ready);
+          publish_sb(x);
+          prescale(x, c + 1);
         } else if (hT) {
           float* hrow = hT + ((static_cast<int64_t>(b) * H + h) * DK + r) * DV + v0 + cb;
 #pragma unroll

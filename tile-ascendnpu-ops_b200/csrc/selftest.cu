@@ -1,10 +1,11 @@
-// Self-test of the bounded-wait path every tensor-core kernel of this library
-// shares (sm100::mbar_wait): a one-warp kernel that holds the same resources a
-// real kernel holds when a wait gives up -- TMEM columns and a bulk copy in
-// flight -- waits on an mbarrier that nothing ever arrives on, and must then
-// take the give-up path exactly as the kernels do: record kErrMbarTimeout in
-// the device error word, let its own copy land (a drain wait), free TMEM and
-// return.  Nothing here can hang: both waits are bounded by the global timer.
+// Self-test of the give-up path the tensor-core kernels of this library take
+// when a wait runs out: a one-warp kernel that holds the same resources a real
+// kernel holds when a wait gives up -- TMEM columns and a bulk copy in flight
+// -- waits on an mbarrier that nothing ever arrives on, and must then do what
+// the kernels do: record kErrMbarTimeout in the device error word, let its
+// own copy land (a drain wait), free TMEM and return.  Its waits are
+// sm100::mbar_wait_polled (test_wait polls against the global timer), which
+// always end; nothing here can hang.
 #include "common.cuh"
 #include "device_error.cuh"
 #include "sm100.cuh"
@@ -24,7 +25,8 @@ struct SelftestSmem {
 
 // out[0] = 1 if the unarmed wait gave up, out[1] = 1 if the drain saw the copy
 // land, out[2] = the sum of the copied bytes (proves the data arrived before
-// the CTA read it), out[3] = 1 once TMEM was released.
+// the CTA read it), out[3] = 1 once TMEM was released, out[4] / out[5] = low /
+// high 32 bits of the nanoseconds the unarmed wait took before giving up.
 __global__ void __launch_bounds__(32, 1)
     selftest_wait_timeout_kernel(const uint8_t* __restrict__ src, int bytes, uint64_t limit_ns,
                                  int* __restrict__ out, int* err) {
@@ -48,11 +50,16 @@ __global__ void __launch_bounds__(32, 1)
     sm100::mbar_arrive_expect_tx(&sm.copy_bar, static_cast<uint32_t>(bytes));
     sm100::bulk_load(sm.buf, src, static_cast<uint32_t>(bytes), &sm.copy_bar);
     // Nothing arrives on never_bar: this wait must give up after limit_ns.
-    const bool got = sm100::mbar_wait(&sm.never_bar, 0, err, &sm.abort_flag, false, limit_ns);
+    const uint64_t t0 = sm100::globaltimer_ns();
+    const bool got =
+        sm100::mbar_wait_polled(&sm.never_bar, 0, err, &sm.abort_flag, false, limit_ns);
+    const uint64_t waited = sm100::globaltimer_ns() - t0;
     out[0] = got ? 0 : 1;
+    out[4] = static_cast<int>(waited & 0xffffffffu);
+    out[5] = static_cast<int>(waited >> 32);
     // The give-up path: the copy issued above still targets shared memory, so
     // wait for it (ignoring the abort flag) before the CTA may exit.
-    landed = sm100::mbar_wait(&sm.copy_bar, 0, err, &sm.abort_flag, true) ? 1 : 0;
+    landed = sm100::mbar_wait_polled(&sm.copy_bar, 0, err, &sm.abort_flag, true) ? 1 : 0;
     out[1] = landed;
   }
   landed = __shfl_sync(0xffffffffu, landed, 0);

@@ -61,18 +61,36 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking test of phase `parity` (never suspends the thread).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
   return t;
 }
 
-// Wait for the phase with the given parity to complete, for at most
-// `limit_ns`.  On timeout: record kErrMbarTimeout in `err` (device global),
-// raise the CTA-wide abort flag and return false.  Also returns false
-// (without waiting) once another thread of the CTA has raised the abort flag.
-// `drain` waits ignore the abort flag (used to let in-flight copies land
-// before the CTA exits).
+// Wait for the phase with the given parity to complete.  The kernels' waits:
+// try_wait lets the hardware park the thread until the phase completes, the
+// fastest way to wait.  Its time limit guards a phase that completes late:
+// after `limit_ns` the wait records kErrMbarTimeout in `err` (device global),
+// raises the CTA-wide abort flag and returns false; it also returns false
+// (without waiting on) once another thread of the CTA has raised the abort
+// flag.  `drain` waits ignore the abort flag (used to let in-flight copies
+// land before the CTA exits).  A phase that never completes is NOT bounded by
+// this wait: a try_wait on such a phase was measured to keep the thread
+// suspended for minutes, with or without a suspend-time hint, so the limit is
+// never checked; mbar_wait_polled below is the wait that does give up.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err,
                                           volatile int* abort_flag, bool drain = false,
                                           uint64_t limit_ns = 2000000000ull) {
@@ -88,6 +106,30 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
         return false;
       }
     }
+  }
+}
+
+// The same contract with a wait that always ends: the phase is polled with
+// the non-blocking test_wait (64 tight polls, then polls 64 ns apart), the
+// global timer read after every poll.  Used where a phase may never complete
+// (the wait self-test); in the kernels' hot loops it was measured 5-11%
+// slower than mbar_wait.
+__device__ __forceinline__ bool mbar_wait_polled(uint64_t* bar, uint32_t parity, int* err,
+                                                 volatile int* abort_flag, bool drain = false,
+                                                 uint64_t limit_ns = 2000000000ull) {
+#pragma unroll 1
+  for (int i = 0; i < 64; ++i)
+    if (mbar_test_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    if (mbar_test_wait(bar, parity)) return true;
+    if (!drain && *abort_flag) return false;
+    if (globaltimer_ns() - t0 > limit_ns) {
+      *abort_flag = 1;
+      report_device_error(err, kErrMbarTimeout);
+      return false;
+    }
+    __nanosleep(64);
   }
 }
 
