@@ -358,8 +358,8 @@ def _gdn() -> Workload:
         beta = torch.sigmoid(torch.randn(B, T, H, generator=g_, device=dev))
         return (q.to(torch.bfloat16), k.to(torch.bfloat16), v.to(torch.bfloat16), g, beta)
 
-    def shard(inp, index, count):
-        sl = bh_split(B, H, index, count)
+    def shard(inp, index, count):  # of these inputs (the whole problem or a rank's part)
+        sl = bh_split(inp[0].shape[0], inp[0].shape[2], index, count)
         if sl is None:
             return None
         bs, hs = sl
@@ -859,13 +859,15 @@ def time_sharded_steps(wl: Workload, op, sets: list, steps: int, warmup: int, wo
             "bytes_total": world * per_rank, "bytes_received_per_rank": (world - 1) * per_rank}
 
 
-def time_e2e(wl: Workload, host_full: tuple, device, steps: int, max_chunks: int = 16) -> dict:
+def time_e2e(wl: Workload, host_full: tuple, device, steps: int, max_chunks: int = 16,
+             copy_streams: int = 1) -> dict:
     """The public op API from pinned host buffers, chunked so that copies in
-    both directions overlap the kernels: per chunk, H2D on one stream, the op
-    on a second, D2H of its outputs on a third.  Returns ms per step (all
-    chunks) and the bytes copied each way."""
+    both directions overlap the kernels: per chunk, H2D on an input stream,
+    the op on the compute stream, D2H of its outputs on an output stream
+    (``copy_streams`` streams each way, chunks dealt round-robin).  Returns ms
+    per step (all chunks) and the bytes copied each way."""
     n_chunks = 1
-    for c in (max_chunks, 8, 4, 2):
+    for c in (max_chunks, 16, 8, 4, 2):
         if c <= max_chunks and wl.shard is not None and wl.shard(host_full, 0, c) is not None:
             n_chunks = c
             break
@@ -886,15 +888,16 @@ def time_e2e(wl: Workload, host_full: tuple, device, steps: int, max_chunks: int
     host_out = [tuple(torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for o in first)
                 for _ in range(n_chunks)]
     del first
-    s_in = torch.cuda.Stream(device)
+    s_ins = [torch.cuda.Stream(device) for _ in range(copy_streams)]
     s_comp = torch.cuda.Stream(device)
-    s_out = torch.cuda.Stream(device)
+    s_outs = [torch.cuda.Stream(device) for _ in range(copy_streams)]
     ev_in = [torch.cuda.Event() for _ in range(n_chunks)]
     ev_done = [torch.cuda.Event() for _ in range(n_chunks)]
     torch.cuda.synchronize(device)
 
     def one_step():
         for i in range(n_chunks):
+            s_in, s_out = s_ins[i % copy_streams], s_outs[i % copy_streams]
             with torch.cuda.stream(s_in):
                 s_in.wait_event(ev_done[i])  # the previous step's call read these buffers
                 for dt, ht in zip(dev_in[i], host_in[i]):
@@ -917,12 +920,14 @@ def time_e2e(wl: Workload, host_full: tuple, device, steps: int, max_chunks: int
     torch.cuda.synchronize(device)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(s_in)
+    e0.record(s_comp)
+    for st in s_ins + s_outs:
+        st.wait_stream(s_comp)
     for _ in range(steps):
         one_step()
-    s_out.wait_stream(s_in)
-    s_out.wait_stream(s_comp)
-    e1.record(s_out)
+    for st in s_ins + s_outs:
+        s_comp.wait_stream(st)
+    e1.record(s_comp)
     torch.cuda.synchronize(device)
     ms = e0.elapsed_time(e1) / steps
     h2d = sum(_nbytes(h) for h in host_in)
@@ -930,7 +935,7 @@ def time_e2e(wl: Workload, host_full: tuple, device, steps: int, max_chunks: int
     return {"ms_per_step": ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "chunks": n_chunks, "calls_per_step": n_chunks,
             "api": f"{type(op).__name__}.__call__ per chunk, pinned host buffers, "
-                   f"H2D / op / D2H on three streams"}
+                   f"H2D / op / D2H on {copy_streams} / 1 / {copy_streams} streams"}
 
 
 def time_cpu(fn: Callable, inputs: tuple, budget_s: float = 10.0) -> tuple[float, int, bool]:
@@ -1052,7 +1057,7 @@ def measure(wl: Workload, args, rank: int, local_rank: int, world: int, device,
     del sets
     torch.cuda.empty_cache()
     e2e_steps = max(3, min(steps, 10))
-    e = time_e2e(wl, host_full, device, e2e_steps, args.e2e_chunks)
+    e = time_e2e(wl, host_full, device, e2e_steps, args.e2e_chunks, args.e2e_streams)
     e2e_ms = max_over_ranks(e["ms_per_step"], world, device)
     rec["e2e"] = {"value": whole_job_value(world * work, 1, e2e_ms, wl.unit), "unit": wl.unit,
                   "h2d_bytes_per_step": e["h2d_bytes_per_step"] * world,
@@ -1229,6 +1234,8 @@ def main() -> None:
                     help="timed calls per op in per_op (the headline uses --steps)")
     ap.add_argument("--e2e-chunks", type=int, default=16,
                     help="chunks per step in the end-to-end leg (at most)")
+    ap.add_argument("--e2e-streams", type=int, default=1,
+                    help="copy streams per direction in the end-to-end leg")
     ap.add_argument("--cpu-budget", type=float, default=10.0,
                     help="seconds of CPU time per op for the CPU baseline")
     ap.add_argument("--no-cpu-baseline", action="store_true")

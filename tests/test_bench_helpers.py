@@ -50,3 +50,19 @@ def test_workload_names_match_the_readme():
     readme = (ROOT / "README.md").read_text()
     for name in bench.workloads():
         assert f"`{name}`" in readme, name
+
+
+def test_gdn_shard_of_a_rank_part_uses_its_own_shape():
+    """The e2e leg chunks a rank's part (2 of the 4 batches at N = 2): the
+    (batch, head) split must follow the part's shape, not the whole problem's."""
+    import torch
+
+    wl = bench.workloads()["gdn"]()
+    part = tuple(torch.arange(2 * 3 * 16 * 4, dtype=torch.float32).view(2, 3, 16, 4)
+                 for _ in range(3)) + tuple(torch.zeros(2, 3, 16) for _ in range(2))
+    pieces = [wl.shard(part, i, 16) for i in range(16)]
+    assert all(p is not None and p[0].shape == (1, 3, 2, 4) for p in pieces)
+    # Every (batch, head) pair appears once, batch-major.
+    got = torch.cat([torch.cat([p[0][:, :, h] for h in range(2)], 0) for p in pieces], 0)
+    want = torch.cat([part[0][b:b + 1, :, h] for b in range(2) for h in range(16)], 0)
+    assert torch.equal(got, want)
