@@ -748,29 +748,35 @@ def _as_tuple(out) -> tuple:
     return tuple(out) if isinstance(out, (tuple, list)) else (out,)
 
 
-def _problem(wl: Workload, device, seed: int, rank: int, world: int) -> tuple:
-    """The rank's part of the problem drawn from ``seed``: the whole problem
-    at N = 1, else the rank's shard of the same full problem."""
+def _problem(wl: Workload, device, seed: int, rank: int, world: int, pieces: int = 1) -> list:
+    """The rank's part of the problem drawn from ``seed`` as a list of input
+    tuples: ``[whole problem]`` at N = 1; else the problem is cut into
+    ``world * pieces`` equal parts and rank r owns parts r, world + r, ...
+    (so the i-th part of every rank, gathered in rank order, is a contiguous
+    run of the whole problem)."""
     full = wl.make_inputs(device, seed)
     if world == 1:
-        return full
-    mine = wl.shard(full, rank, world) if wl.shard else None
-    if mine is None:
-        raise RuntimeError(f"{wl.name}: the problem does not split into {world} equal shards")
+        return [full]
+    count = world * pieces
+    mine = [wl.shard(full, i * world + rank, count) if wl.shard else None
+            for i in range(pieces)]
+    if any(m is None for m in mine):
+        raise RuntimeError(f"{wl.name}: the problem does not split into {count} equal parts")
     del full
     return mine
 
 
 # -------------------------------------------------------------- timing legs
-def time_calls(wl: Workload, op, sets: list, steps: int, warmup: int, graph: bool,
+def time_calls(run: Callable, sets: list, steps: int, warmup: int, graph: bool,
                device, stream) -> dict:
-    """K op calls over rotating input sets: graph replays (or eager calls)
-    with CUDA events around each; returns total and mean per-call ms."""
+    """K steps over rotating input sets, a step being ``run(set)`` (the op on
+    every part of the rank's problem): graph replays (or eager steps) with
+    CUDA events around each; returns total and mean per-step ms."""
     n_sets = len(sets)
     for i in range(warmup):
-        wl.run(op, sets[i % n_sets])
+        run(sets[i % n_sets])
     torch.cuda.synchronize(device)
-    out_bytes = max(1, _nbytes(_as_tuple(wl.run(op, sets[0]))))
+    out_bytes = max(1, _nbytes(run(sets[0])))
     per_graph = max(1, min(64, (8 << 30) // out_bytes) // n_sets) * n_sets
     per_graph = min(per_graph, steps)
 
@@ -779,7 +785,7 @@ def time_calls(wl: Workload, op, sets: list, steps: int, warmup: int, graph: boo
         keep = []
         with torch.cuda.graph(g):
             for i in range(n):
-                keep.append(wl.run(op, sets[i % n_sets]))
+                keep.append(run(sets[i % n_sets]))
         del keep
         return g
 
@@ -797,7 +803,7 @@ def time_calls(wl: Workload, op, sets: list, steps: int, warmup: int, graph: boo
             g_main.replay()
         torch.cuda.synchronize(device)
     else:
-        chunks = [((lambda inp=sets[i % n_sets]: wl.run(op, inp)), 1) for i in range(steps)]
+        chunks = [((lambda inp=sets[i % n_sets]: run(inp)), 1) for i in range(steps)]
     starts = [torch.cuda.Event(enable_timing=True) for _ in chunks]
     ends = [torch.cuda.Event(enable_timing=True) for _ in chunks]
     torch.cuda.synchronize(device)
@@ -815,19 +821,39 @@ def time_calls(wl: Workload, op, sets: list, steps: int, warmup: int, graph: boo
 
 def time_sharded_steps(wl: Workload, op, sets: list, steps: int, warmup: int, world: int,
                        device, stream) -> dict:
-    """K steps of (op on this rank's shard, then every output gathered on
-    every rank and put back in the full layout), eager, CUDA events around
-    all K steps on the launching stream."""
-    n_sets = len(sets)
-    outs = _as_tuple(wl.run(op, sets[0]))
-    check_shard_shapes([tuple(o.shape) for o in outs], world, device)
-    fulls = gather_outputs(outs, world, device)
+    """K steps of (the op on each part this rank owns, every part's outputs
+    gathered on every rank as soon as that part is done, then the full layout
+    back), eager, CUDA events around all K steps on the launching stream.
+    With several parts the gather of part i (NCCL, asynchronous) runs while
+    the op computes part i + 1."""
+    import torch.distributed as dist
+
+    n_sets, parts = len(sets), len(sets[0])
+    outs = [_as_tuple(wl.run(op, part)) for part in sets[0]]
+    check_shard_shapes([tuple(o.shape) for o in outs[0]], world, device)
+    numels = [o.numel() for o in outs[0]]
+    fulls = [torch.empty(world * parts * n, dtype=o.dtype, device=device)
+             for o, n in zip(outs[0], numels)]
+
+    def gather_part(i, res):
+        works = []
+        for full, o, n in zip(fulls, res, numels):
+            dst = full[i * world * n:(i + 1) * world * n]
+            works.append(dist.all_gather_into_tensor(dst, o.contiguous().view(-1),
+                                                     async_op=True))
+        return works
+
+    def finish(works):
+        for w in works:
+            w.wait()
+        if wl.unshard is not None:
+            wl.unshard(fulls, world * parts)
 
     def step(i):
-        res = _as_tuple(wl.run(op, sets[i % n_sets]))
-        gathered = gather_outputs(res, world, device, fulls)
-        if wl.unshard is not None:
-            wl.unshard(gathered, world)
+        works = []
+        for j, part in enumerate(sets[i % n_sets]):
+            works += gather_part(j, _as_tuple(wl.run(op, part)))
+        finish(works)
 
     for i in range(max(1, warmup)):
         step(i)
@@ -848,15 +874,17 @@ def time_sharded_steps(wl: Workload, op, sets: list, steps: int, warmup: int, wo
     reps = max(3, min(steps, 10))
     g0.record(stream)
     for _ in range(reps):
-        gathered = gather_outputs(outs, world, device, fulls)
-        if wl.unshard is not None:
-            wl.unshard(gathered, world)
+        works = []
+        for j in range(parts):
+            works += gather_part(j, outs[j])
+        finish(works)
     g1.record(stream)
     torch.cuda.synchronize(device)
     gather_ms = g0.elapsed_time(g1) / reps
-    per_rank = _nbytes(outs)
+    per_rank = sum(_nbytes(o) for o in outs)
     return {"step_ms": step_ms, "gather_ms": gather_ms, "bytes_per_rank": per_rank,
-            "bytes_total": world * per_rank, "bytes_received_per_rank": (world - 1) * per_rank}
+            "bytes_total": world * per_rank, "bytes_received_per_rank": (world - 1) * per_rank,
+            "parts_per_rank": parts}
 
 
 def time_e2e(wl: Workload, host_full: tuple, device, steps: int, max_chunks: int = 16,
@@ -920,16 +948,25 @@ def time_e2e(wl: Workload, host_full: tuple, device, steps: int, max_chunks: int
     torch.cuda.synchronize(device)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
+    # One copy stream each way: the end of every step (its last D2H) is
+    # stamped on the output stream, and the step time is the median interval
+    # between consecutive stamps (steady state; a host hiccup of one step
+    # does not move it).  Several copy streams: the mean over all steps.
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     e0.record(s_comp)
     for st in s_ins + s_outs:
         st.wait_stream(s_comp)
-    for _ in range(steps):
+    for i in range(steps):
         one_step()
+        if copy_streams == 1:
+            ends[i].record(s_outs[0])
     for st in s_ins + s_outs:
         s_comp.wait_stream(st)
     e1.record(s_comp)
     torch.cuda.synchronize(device)
     ms = e0.elapsed_time(e1) / steps
+    if copy_streams == 1 and steps >= 3:
+        ms = statistics.median(a.elapsed_time(b) for a, b in zip(ends[:-1], ends[1:]))
     h2d = sum(_nbytes(h) for h in host_in)
     d2h = sum(_nbytes(h) for h in host_out)
     return {"ms_per_step": ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
@@ -989,23 +1026,32 @@ def measure(wl: Workload, args, rank: int, local_rank: int, world: int, device,
     """Every leg of one op: kernel-only replays, the sharded step with its
     reassembly (N > 1), the end-to-end host path, and the CPU baseline."""
     stream = torch.cuda.current_stream(device)
-    probe = _problem(wl, device, SEED, rank, world)
-    op = wl.build_op(probe)
-    set_bytes = _nbytes(probe) + _nbytes(_as_tuple(wl.run(op, probe)))
+    pieces = args.pieces if world > 1 else 1
+    try:
+        probe = _problem(wl, device, SEED, rank, world, pieces)
+    except RuntimeError:
+        pieces = 1
+        probe = _problem(wl, device, SEED, rank, world, pieces)
+    op = wl.build_op(probe[0])
+
+    def run(parts):  # the op on every part of this rank's problem
+        return tuple(o for part in parts for o in _as_tuple(wl.run(op, part)))
+
+    set_bytes = sum(_nbytes(p) for p in probe) + _nbytes(run(probe))
     n_sets = max(2, min(32, -(-3 * L2_BYTES // max(set_bytes, 1)) + 1))
-    sets = [probe] + [_problem(wl, device, SEED + 1000 * i, rank, world)
+    sets = [probe] + [_problem(wl, device, SEED + 1000 * i, rank, world, pieces)
                       for i in range(1, n_sets)]
-    work = wl.work(op)  # one call on this rank's part
+    work = wl.work(op) * pieces  # this rank's part (all its pieces)
     peaks, peak_kind = load_peaks()
     roof_unit = wl.roof_unit or wl.unit
-    roof_work = wl.roof_work(op) if wl.roof_work else work
+    roof_work = wl.roof_work(op) * pieces if wl.roof_work else work
     peak, peak_unit = _peak(roof_unit, peaks)
     steps = args.steps if headline else min(args.steps, args.per_op_steps)
 
     sampler = ClockSampler(local_rank)
     barrier(world, device)
     with sampler:
-        k = time_calls(wl, op, sets, steps, args.warmup, args.graph, device, stream)
+        k = time_calls(run, sets, steps, args.warmup, args.graph, device, stream)
         sharded = None
         if world > 1:
             sharded = time_sharded_steps(wl, op, sets, steps, args.warmup, world, device,
@@ -1041,31 +1087,42 @@ def measure(wl: Workload, args, rank: int, local_rank: int, world: int, device,
         rec["kernel_only"] = {
             "value": whole_job_value(world * work, 1, per_call_ms, wl.unit),
             "ms_per_step": per_call_ms,
-            "note": "the shard op alone, graph replays, slowest rank"}
+            "note": "the op on this rank's parts alone, graph replays, slowest rank"}
         rec["gather"] = {
-            "collective": "all_gather_into_tensor per output (NCCL), then the full layout",
+            "collective": "all_gather_into_tensor per output and part (NCCL, asynchronous: "
+                          "part i is gathered while part i + 1 computes), then the full layout",
+            "parts_per_rank": sharded["parts_per_rank"],
             "ms": gather_ms, "bytes_per_rank": sharded["bytes_per_rank"],
             "bytes_total": sharded["bytes_total"],
             "bytes_received_per_rank": sharded["bytes_received_per_rank"],
             "busbw_GBps": sharded["bytes_received_per_rank"] / (gather_ms * 1e-3) / 1e9}
-        rec["config"]["parallelism"] = (f"{wl.shard_desc} split over {world} ranks (same seed, "
-                                        "sliced) + NCCL all_gather_into_tensor reassembly")
+        rec["config"]["parallelism"] = (
+            f"{wl.shard_desc} split into {world} x {pieces} parts (same seed, sliced; rank r "
+            f"owns parts r, {world} + r, ...) + NCCL all_gather_into_tensor reassembly"
+            + (" overlapping the next part's op" if pieces > 1 else ""))
     rec["clocks"] = sampler.summary()
 
-    # End to end through the public API from pinned host buffers.
-    host_full = tuple(t.cpu() if isinstance(t, torch.Tensor) else t for t in sets[0])
+    # End to end through the public API from pinned host buffers: every part
+    # of this rank's problem in turn.
+    host_parts = [tuple(t.cpu() if isinstance(t, torch.Tensor) else t for t in part)
+                  for part in sets[0]]
     del sets
     torch.cuda.empty_cache()
     e2e_steps = max(3, min(steps, 10))
-    e = time_e2e(wl, host_full, device, e2e_steps, args.e2e_chunks, args.e2e_streams)
-    e2e_ms = max_over_ranks(e["ms_per_step"], world, device)
+    e2e_ms, h2d, d2h = 0.0, 0, 0
+    for hp in host_parts:
+        e = time_e2e(wl, hp, device, e2e_steps, args.e2e_chunks, args.e2e_streams)
+        e2e_ms += e["ms_per_step"]
+        h2d += e["h2d_bytes_per_step"]
+        d2h += e["d2h_bytes_per_step"]
+    e2e_ms = max_over_ranks(e2e_ms, world, device)
     rec["e2e"] = {"value": whole_job_value(world * work, 1, e2e_ms, wl.unit), "unit": wl.unit,
-                  "h2d_bytes_per_step": e["h2d_bytes_per_step"] * world,
-                  "d2h_bytes_per_step": e["d2h_bytes_per_step"] * world, "ms_per_step": e2e_ms,
-                  "chunks_per_rank": e["chunks"], "api": e["api"]}
+                  "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
+                  "ms_per_step": e2e_ms, "chunks_per_rank": e["chunks"] * len(host_parts),
+                  "api": e["api"]}
     if with_cpu and world == 1 and wl.cpu_ref is not None and rank == 0:
-        rec["cpu_baseline"] = cpu_baseline(wl, host_full, work, args.cpu_budget)
-    del host_full, probe, op
+        rec["cpu_baseline"] = cpu_baseline(wl, host_parts[0], work, args.cpu_budget)
+    del host_parts, probe, op
     torch.cuda.empty_cache()
     return rec
 
@@ -1108,8 +1165,9 @@ def run_ours(args) -> Optional[dict]:
         n_sets = max(2, min(32, -(-3 * L2_BYTES // max(_nbytes(full) * 2, 1)) + 1))
         sets = [full] + [wl.make_inputs(device, SEED + rank + 1000 * i) for i in range(1, n_sets)]
         barrier(world, device)
-        k = time_calls(wl, op, sets, min(args.steps, args.per_op_steps), args.warmup, args.graph,
-                       device, torch.cuda.current_stream(device))
+        k = time_calls(lambda inp: _as_tuple(wl.run(op, inp)), sets,
+                       min(args.steps, args.per_op_steps), args.warmup, args.graph, device,
+                       torch.cuda.current_stream(device))
         barrier(world, device)
         ms = max_over_ranks(k["per_call_ms"], world, device)
         weak = {"value": whole_job_value(world * wl.work(op), 1, ms, wl.unit),
@@ -1234,6 +1292,10 @@ def main() -> None:
                     help="timed calls per op in per_op (the headline uses --steps)")
     ap.add_argument("--e2e-chunks", type=int, default=16,
                     help="chunks per step in the end-to-end leg (at most)")
+    ap.add_argument("--pieces", type=int, default=1,
+                    help="N > 1: parts per rank; each part's outputs are gathered while the "
+                         "next part computes (1 = one shard per rank, gathered after it; "
+                         "measured faster than 2 or 4 parts at N = 2)")
     ap.add_argument("--e2e-streams", type=int, default=1,
                     help="copy streams per direction in the end-to-end leg")
     ap.add_argument("--cpu-budget", type=float, default=10.0,

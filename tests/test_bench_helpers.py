@@ -66,3 +66,24 @@ def test_gdn_shard_of_a_rank_part_uses_its_own_shape():
     got = torch.cat([torch.cat([p[0][:, :, h] for h in range(2)], 0) for p in pieces], 0)
     want = torch.cat([part[0][b:b + 1, :, h] for b in range(2) for h in range(16)], 0)
     assert torch.equal(got, want)
+
+
+def test_parts_of_every_rank_gathered_in_rank_order_rebuild_the_problem():
+    """At N ranks with P parts each, rank r owns parts r, N + r, ...: gathering
+    part i of every rank in rank order is a contiguous run of the problem."""
+    import torch
+
+    wl = bench.Workload(
+        name="toy", metric="", unit="GB/s", dtype="f32", config={},
+        make_inputs=lambda dev, seed: (torch.arange(48.0).view(24, 2), torch.ones(3)),
+        build_op=lambda inp: None, run=lambda op, inp: inp[0], work=lambda op: 0.0,
+        kernel_regex="", shard=bench._rows_shard(1))
+    world, pieces = 3, 2
+    per_rank = [bench._problem(wl, torch.device("cpu"), 0, r, world, pieces)
+                for r in range(world)]
+    rebuilt = torch.cat([per_rank[r][i][0] for i in range(pieces) for r in range(world)])
+    assert torch.equal(rebuilt, torch.arange(48.0).view(24, 2))
+    assert all(torch.equal(p[1], torch.ones(3)) for parts in per_rank for p in parts)
+    with pytest.raises(RuntimeError):
+        bench._problem(wl, torch.device("cpu"), 0, 0, world, 5)  # 24 rows / 15 parts
+    assert len(bench._problem(wl, torch.device("cpu"), 0, 0, 1, 2)) == 1  # N = 1: whole

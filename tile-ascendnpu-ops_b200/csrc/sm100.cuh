@@ -112,7 +112,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
 // The same contract with a wait that always ends: the phase is polled with
 // the non-blocking test_wait (64 tight polls, then polls 64 ns apart), the
 // global timer read after every poll.  Used where a phase may never complete
-// (the wait self-test); in the kernels' hot loops it was measured 5-11%
+// (the wait self-test); in the kernels' hot loops it was measured 5-10%
 // slower than mbar_wait.
 __device__ __forceinline__ bool mbar_wait_polled(uint64_t* bar, uint32_t parity, int* err,
                                                  volatile int* abort_flag, bool drain = false,
