@@ -18,6 +18,11 @@
 //                    query row r of its tile (= TMEM lane r)
 //   warp 8           TMA producer: Q0, Q1 once, then K_j / V_j (2-stage rings)
 //   warp 9           MMA issuer (one thread) + TMEM owner
+//   warps 10, 11     idle (they complete the third warpgroup, so that the
+//                    register split below is the same on every SM
+//                    sub-partition)
+// setmaxnreg moves registers from the TMA / MMA warpgroup (72 each) to the
+// softmax warpgroups (216 each), which hold a whole row of S.
 // TMEM (512 columns): tile t uses [256t, 256t+128) for S_t, then P_t (bf16
 // pairs, written over the first 64 columns once S_t is in registers), and
 // [256t+128, 256t+128+D) for the O_t accumulator.
@@ -29,11 +34,11 @@
 // its softmax.  tcgen05 ops of one thread complete in issue order, so the
 // commit that signals "S_t,j done" also means "PV_t,j-1 done": the softmax
 // warps may then rescale O_t in TMEM and overwrite S_t with P_t.
-// Softmax: the running max moves (and O is rescaled) only when it grows by
-// more than 8 in log2 units, so P <= 256 and rescales are rare; exp2 is
-// ex2.approx on exp2(scale*log2e*s - m), the FMA and the row sum as packed
-// f32x2 instructions; each pass over S keeps the next 32-column TMEM load in
-// flight while the current one is processed.
+// Softmax: one TMEM pass puts the block's 128 scores of a row in registers;
+// the running max moves (and O is rescaled) only when it grows by more than 8
+// in log2 units, so P <= 256 and rescales are rare; exp2 is ex2.approx on
+// exp2(scale*log2e*s - m), the FMA and the row sum as packed f32x2
+// instructions; P is stored 32 scores at a time.
 // Every mbarrier wait is bounded (2 s): on timeout the kernel records an
 // error (tileops_device_error_flag), drains its copies / MMAs, frees TMEM and
 // returns.
@@ -56,7 +61,16 @@ constexpr int kTiles = 2;
 constexpr int kBN = 128;  // keys per block
 constexpr int kStages = 2;  // K and V ring depth
 constexpr int kSoftmaxThreads = 128 * kTiles;
-constexpr int kThreads = kSoftmaxThreads + 64;
+constexpr int kThreads = kSoftmaxThreads + 128;  // + one warpgroup: TMA, MMA, two idle warps
+// Register split (setmaxnreg): launched at kLaunchRegs per thread, the
+// TMA / MMA warpgroup gives registers back and the softmax warpgroups take
+// them, so a softmax thread holds a whole row of S.  Per SM sub-partition
+// (one warp of each warpgroup): 2 x 216 + 72 = 3 x 168.
+constexpr int kLaunchRegs = 168;
+constexpr int kSoftmaxRegs = 216;
+constexpr int kProducerRegs = 72;
+static_assert(kTiles * 4 * kSoftmaxRegs + 4 * kProducerRegs == (kThreads / 32) * kLaunchRegs,
+              "register split must equal the launch allocation");
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 constexpr int kGroupBH = 16;  // (b, h) pairs per launch-order group
@@ -172,6 +186,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t kTileBytes = L::kTile;
   constexpr int kChunks = D / 64;  // 64-wide (128-byte) column chunks of a tile
 
+  if (warp >= 8) reg_dealloc<kProducerRegs>();
   if (warp == 8) {
     // ------------------------------------------------------ TMA producer
     if (lane == 0 && nblk > 0) {
@@ -269,8 +284,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mma_commit(&bars->mma_drain);
       mbar_wait(&bars->mma_drain, 0, p.err, abort_flag, true);
     }
-  } else {
+  } else if (warp < 8) {
     // ------------------------------------- softmax warpgroups (warps 0..7)
+    reg_alloc<kSoftmaxRegs>();
     const int t = warp >> 2;                 // tile of this warpgroup
     const int row = threadIdx.x & 127;       // row within the tile == TMEM lane
     const int q0 = q_cta + t * kBM;
@@ -292,31 +308,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool need_mask = (k0 + kBN > p.seq_kv) || (p.causal && k0 + kBN - 1 > q0 + off);
       // Keys this row may see in the block: [k0, k0 + nvis).
       const int nvis = need_mask ? max(0, min(kBN, min(p.seq_kv - 1, row_limit) + 1 - k0)) : kBN;
-      // Pass 1: row max of the raw scores (scale > 0 commutes with max), 8
-      // chains; the TMEM load of 32-column chunk c+1 is in flight while chunk
-      // c is reduced.
+      // The block's scores of this row, all four 32-column loads in flight at once.
+      uint32_t sc[kBN / 32][32];
+#pragma unroll
+      for (int c = 0; c < kBN / 32; ++c) tmem_ld32(t_s + c * 32, sc[c]);
+#pragma unroll
+      for (int c = 0; c < kBN / 32; ++c) tmem_wait_ld_regs(sc[c]);
+      // Row max of the raw scores (scale > 0 commutes with max), 8 chains.
       float mx[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) mx[i] = -INFINITY;
-      {
-        uint32_t ra[32], rb[32];
-        tmem_ld32(t_s, ra);
-        tmem_wait_ld_regs(ra);
+      if (!need_mask) {
 #pragma unroll
-        for (int c = 0; c < kBN / 32; ++c) {
-          uint32_t(&cur)[32] = (c & 1) ? rb : ra;
-          uint32_t(&nxt)[32] = (c & 1) ? ra : rb;
-          if (c + 1 < kBN / 32) tmem_ld32(t_s + (c + 1) * 32, nxt);
-          if (!need_mask) {
+        for (int c = 0; c < kBN / 32; ++c)
 #pragma unroll
-            for (int i = 0; i < 32; ++i) mx[i & 7] = fmaxf(mx[i & 7], __uint_as_float(cur[i]));
-          } else {
+          for (int i = 0; i < 32; ++i) mx[i & 7] = fmaxf(mx[i & 7], __uint_as_float(sc[c][i]));
+      } else {
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (c * 32 + i < nvis) mx[i & 7] = fmaxf(mx[i & 7], __uint_as_float(cur[i]));
-          }
-          if (c + 1 < kBN / 32) tmem_wait_ld_regs(nxt);
-        }
+        for (int c = 0; c < kBN / 32; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (c * 32 + i < nvis) mx[i & 7] = fmaxf(mx[i & 7], __uint_as_float(sc[c][i]));
       }
       const float mraw = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
                                fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
@@ -324,10 +336,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       float m_use = m;
       if (mloc > m + kRescaleThreshold || m == -INFINITY) m_use = fmaxf(mloc, m);
       const float m_sub = (m_use == -INFINITY) ? 0.0f : m_use;
-      // O_t is idle here (PV_t,j-1 completed before S_t,j): rescale if the max moved.
-      if (j > 0 && m_use != m) {
-        const float alpha = ex2(m - m_use);
-#pragma unroll
+      const float m_prev = m;
+      m = m_use;
+      // O_t is idle here (PV_t,j-1 completed before S_t,j; PV_t,j waits for
+      // this block's P): rescale the rows whose max moved.  The whole warp
+      // takes the branch (tcgen05.ld / st are .sync.aligned); alpha = 1 leaves
+      // the other rows as they are.
+      if (j > 0 && __any_sync(0xffffffffu, m_use != m_prev)) {
+        const float alpha = m_use != m_prev ? ex2(m_prev - m_use) : 1.0f;
+#pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {
           uint32_t r[32];
           tmem_ld32(t_o + c * 32, r);
@@ -338,28 +355,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         l *= alpha;
       }
-      m = m_use;
-      // Pass 2: P = exp2(scale*log2e*s - m) two scores at a time (packed
-      // f32x2 FMA and add), packed to 16-bit pairs over S columns already
-      // read; chunk c+1's TMEM load overlaps chunk c's exponentials.
+      // P = exp2(scale*log2e*s - m) two scores at a time (packed f32x2 FMA
+      // and add), packed to 16-bit pairs over S columns [0, 64).
       float2 ps[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
       {
         const float2 scale2 = make_float2(sl2, sl2), negm2 = make_float2(-m_sub, -m_sub);
-        uint32_t ra[32], rb[32];
-        tmem_ld32(t_s, ra);
-        tmem_wait_ld_regs(ra);
 #pragma unroll
         for (int c = 0; c < kBN / 32; ++c) {
-          uint32_t(&cur)[32] = (c & 1) ? rb : ra;
-          uint32_t(&nxt)[32] = (c & 1) ? ra : rb;
-          if (c + 1 < kBN / 32) tmem_ld32(t_s + (c + 1) * 32, nxt);
           uint32_t pk[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const int kk = c * 32 + 2 * i;
             const float2 x = ffma2(
-                make_float2(__uint_as_float(cur[2 * i]), __uint_as_float(cur[2 * i + 1])), scale2,
-                negm2);
+                make_float2(__uint_as_float(sc[c][2 * i]), __uint_as_float(sc[c][2 * i + 1])),
+                scale2, negm2);
             float e0 = ex2(x.x), e1 = ex2(x.y);
             if (need_mask) {
               e0 = kk < nvis ? e0 : 0.0f;
@@ -368,9 +377,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ps[i & 1] = fadd2(ps[i & 1], make_float2(e0, e1));
             pk[i] = pack2(e0, e1, BF16);
           }
-          // P columns [16c, 16c+16) lie in S columns already read.
           tmem_st16(t_s + c * 16, pk);
-          if (c + 1 < kBN / 32) tmem_wait_ld_regs(nxt);
         }
       }
       const float rowsum = (ps[0].x + ps[1].x) + (ps[0].y + ps[1].y);
@@ -438,6 +445,13 @@ int launch_attn(const void* q, const void* k, const void* v, void* o, float* lse
   p.err = device_error_ptr();
   auto kern = attn_fwd_kernel<D, BF16>;
   const int smem = Smem<D>::kAlloc;
+  // The setmaxnreg split assumes exactly kLaunchRegs registers per thread at
+  // launch; with fewer the increases could never be granted.
+  static const bool regs_ok = [kern] {
+    cudaFuncAttributes a;
+    return cudaFuncGetAttributes(&a, kern) == cudaSuccess && a.numRegs == kLaunchRegs;
+  }();
+  if (!regs_ok) return TILEOPS_ELAUNCH;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
       cudaSuccess)
     return TILEOPS_ELAUNCH;
