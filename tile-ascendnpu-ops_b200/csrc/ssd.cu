@@ -27,10 +27,13 @@
 // Epilogue: out = exp(dA[l]) D1 + D2 straight from TMEM to global fp32.
 // Every mbarrier wait is bounded (2 s); a timeout sets the device error flag,
 // the MMAs issued so far are drained and TMEM is freed before returning.
+#include <cudaTypedefs.h>
+
 #include <type_traits>
 
 #include "common.cuh"
 #include "sm100.cuh"
+#include "tma_host.cuh"
 
 namespace tileops {
 namespace {
@@ -52,9 +55,10 @@ __device__ __forceinline__ uint32_t ssd_swz(int r, int u) {
 
 // Shared-memory layout, sized per call (offsets in bytes from a 1 KB-aligned
 // base, every tile 1 KB aligned): C [128][nc64] and prev [P][nc64] K-major
-// (nc64 = d_state rounded up to 64-column chunks), two W blocks [128][64],
-// three x blocks [64][pc64] MN-major (pc64 = d_head rounded up to 64), dA and
-// dt of the chunk, the barriers.
+// (nc64 = d_state rounded up to 64-column chunks), two cb / W blocks
+// [128][64], three x blocks [64][pc64] MN-major (pc64 = d_head rounded up to
+// 64), dA and dt of the chunk, the barriers.  The third cb / W block lives in
+// the C tile once the history MMA has read it.
 struct SsdLayout {
   int c, prev, w, x, da, dt, rng, bar, bytes;
   int x_stride;  // bytes of one x block
@@ -66,16 +70,25 @@ struct SsdLayout {
     w = up1k(prev + P * nc64 * 2);
     x = w + 2 * kSsdRows * kSsdKBlk * 2;
     x_stride = kSsdKBlk * pc64 * 2;
+    // dA and dt of the chunk, each starting on a 16-byte boundary (the W
+    // build reads them as float4).
     da = up1k(x + 3 * x_stride);
-    dt = da + Q * 4;
-    rng = dt + Q * 4;  // per 64-key block: min, max of dA (2 x 16 floats)
+    dt = da + ((Q * 4 + 15) & ~15);
+    rng = dt + ((Q * 4 + 15) & ~15);  // per 64-key block: min, max of dA (2 x 16 floats)
     bar = up1k(rng + 2 * 16 * 4);
     bytes = bar + 64;
+  }
+  // cb / W block buffer i (0, 1: dedicated; 2: the C tile).
+  __host__ __device__ int wbuf(int i) const {
+    return i == 2 ? c : w + i * (kSsdRows * kSsdKBlk * 2);
   }
 };
 
 struct SsdBars {
-  uint64_t blk_done[2];  // MMAs of the W / x block in buffer i completed
+  uint64_t full[3];      // tensor-copy path: x and cb of the block in buffer i landed
+  uint64_t c_full;       // tensor-copy path: the C tile landed
+  uint64_t blk_done[3];  // MMAs of the cb / W and x blocks in buffer i completed
+  uint64_t d1_done;      // the history MMA completed (the C tile may be reused)
   uint64_t all_done;     // every MMA completed
   uint32_t tmem_base;
   int abort_flag;
@@ -126,8 +139,18 @@ struct SsdParams {
   int* err;
 };
 
-template <typename T>
-__global__ void __launch_bounds__(kSsdThreads, 2) ssd_chunk_scan(const SsdParams p) {
+// kTma: the C tile, x blocks and cb blocks are brought by tensor copies
+// (one thread, completion on mbarriers) instead of 16-byte cp.async from
+// every thread, which keeps the SM's load / shared-memory pipeline free for
+// the W build; requires chunk length, d_head and d_state multiples of 64.
+// With kTma and a chunk length that is a multiple of 128 (no row tile
+// reaches into the next chunk) the output leaves by tensor stores too.
+template <typename T, bool kTma>
+__global__ void __launch_bounds__(kSsdThreads, 2)
+    ssd_chunk_scan(const SsdParams p, const __grid_constant__ CUtensorMap tm_x,
+                   const __grid_constant__ CUtensorMap tm_c,
+                   const __grid_constant__ CUtensorMap tm_cb,
+                   const __grid_constant__ CUtensorMap tm_out) {
   const SsdLayout L(p.P, p.N, p.Q);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>(
@@ -156,8 +179,12 @@ __global__ void __launch_bounds__(kSsdThreads, 2) ssd_chunk_scan(const SsdParams
   const int nblk = (kend + kSsdKBlk - 1) / kSsdKBlk;
 
   if (tid == 0) {
-    mbar_init(&bars->blk_done[0], 1);
-    mbar_init(&bars->blk_done[1], 1);
+    for (int i = 0; i < 3; ++i) {
+      mbar_init(&bars->full[i], 1);
+      mbar_init(&bars->blk_done[i], 1);
+    }
+    mbar_init(&bars->c_full, 1);
+    mbar_init(&bars->d1_done, 1);
     mbar_init(&bars->all_done, 1);
     bars->abort_flag = 0;
     fence_mbar_init();
@@ -169,37 +196,85 @@ __global__ void __launch_bounds__(kSsdThreads, 2) ssd_chunk_scan(const SsdParams
     tmem_relinquish();
   }
 
-  // ---- per-chunk scalars: dA (fp32) and dt -> shared
   const int64_t hc = (static_cast<int64_t>(b) * p.H + h) * p.NC + c;
-  // dA is kept in log2 units: exp(a - b) = ex2(a' - b').
-  for (int i = tid; i < Q; i += kSsdThreads) {
-    sdA[i] = p.dA[hc * Q + i] * 1.4426950408889634f;
-    sdt[i] = Cvt<T>::to_f(static_cast<const T*>(p.dt)[hc * Q + i]);
-  }
-
   const T* xg = static_cast<const T*>(p.x);
   const T* cbg = static_cast<const T*>(p.cb) +
                  ((static_cast<int64_t>(b) * p.NC + c) * p.G + g) * static_cast<int64_t>(Q) * Q;
-  // Thread layout of a W block: packet column cpk (keys 8 cpk.. of the
-  // block) of rows rg + kSsdRowGroups it.
+  const float* pg = p.prev + ((static_cast<int64_t>(b) * p.NC + c) * p.H + h) * P * N;
+  const int pupr = npad / 8, ptotal = P * pupr;  // 16-byte units of prev rows (as dtype)
+
+  // ---- prologue: every global load of the CTA's first two blocks in flight
+  // at once (prev and dA / dt into registers, C, x and cb by cp.async).
+  float4 va[8], vb[8];  // this thread's first eight prev packets (fp32)
+  auto load_prev = [&](int base) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int i = base + k * kSsdThreads + tid;
+      va[k] = vb[k] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      if (i < ptotal) {
+        const int r = static_cast<int>(p.div_c.div(i)), n = (i - r * pupr) * 8;
+        if (n < N) {
+          const float* src = pg + static_cast<int64_t>(r) * N + n;
+          va[k] = __ldcs(reinterpret_cast<const float4*>(src));
+          vb[k] = __ldcs(reinterpret_cast<const float4*>(src + 4));
+        }
+      }
+    }
+  };
+  auto store_prev = [&](int base) {  // -> dtype, K-major [p][n]
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int i = base + k * kSsdThreads + tid;
+      if (i < ptotal) {
+        const int r = static_cast<int>(p.div_c.div(i)), n = (i - r * pupr) * 8;
+        uint4 pk;
+        pk.x = pack16<T>(va[k].x, va[k].y);
+        pk.y = pack16<T>(va[k].z, va[k].w);
+        pk.z = pack16<T>(vb[k].x, vb[k].y);
+        pk.w = pack16<T>(vb[k].z, vb[k].w);
+        *reinterpret_cast<uint4*>(sm + L.prev + (n >> 6) * (P * 128) +
+                                  ssd_swz(r, (n & 63) >> 3)) = pk;
+      }
+    }
+  };
+  load_prev(0);
+  constexpr int kMaxQPerThread = kSsdMaxQ / kSsdThreads;
+  float rdA[kMaxQPerThread], rdt[kMaxQPerThread];
+#pragma unroll
+  for (int k = 0; k < kMaxQPerThread; ++k) {
+    const int i = tid + k * kSsdThreads;
+    if (i < Q) {
+      rdA[k] = p.dA[hc * Q + i];
+      rdt[k] = Cvt<T>::to_f(static_cast<const T*>(p.dt)[hc * Q + i]);
+    }
+  }
+
+  // Thread layout of a cb / W block: packet column cpk (keys 8 cpk.. of the
+  // block) of rows rg + kSsdRowGroups it; the thread that copies a packet is
+  // the one that turns it into W, so no barrier separates the two.
   const int cpk = tid & 7, rg = tid >> 3;
   const bool cbvec = (Q & 7) == 0;
-  uint4 cbr[kSsdRows / kSsdRowGroups];  // this thread's cb packets of the next W block
-  auto load_cb = [&](int j) {  // global -> registers, all eight in flight
+  auto issue_cb = [&](int j) {  // cb rows of key block j -> cb / W buffer j % 3
     const int sc = j * kSsdKBlk + cpk * 8;
+    uint8_t* dst = sm + L.wbuf(j % 3);
 #pragma unroll
     for (int it = 0; it < kSsdRows / kSsdRowGroups; ++it) {
-      const int l = l0 + rg + kSsdRowGroups * it;
-      cbr[it] = make_uint4(0u, 0u, 0u, 0u);
-      if (l < Q && sc <= l) {
-        const T* row = cbg + static_cast<int64_t>(l) * Q + sc;
-        if (cbvec && sc + 8 <= Q) {
-          cbr[it] = __ldg(reinterpret_cast<const uint4*>(row));
-        } else {
-          T* cv = reinterpret_cast<T*>(&cbr[it]);
+      const int r = rg + kSsdRowGroups * it;
+      const int l = l0 + r;
+      // Packets wholly above the diagonal, past the chunk, or of rows past
+      // the chunk are zero.
+      const bool ok = l < Q && sc <= l && sc < Q;
+      const T* row = cbg + static_cast<int64_t>(ok ? l : 0) * Q + (ok ? sc : 0);
+      if (cbvec) {
+        cp_async16(sb + L.wbuf(j % 3) + ssd_swz(r, cpk), row, ok);
+      } else {
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (ok) {
+          T* cv = reinterpret_cast<T*>(&v);
 #pragma unroll
           for (int e = 0; e < 8; ++e) cv[e] = sc + e < Q ? row[e] : Cvt<T>::from_f(0.0f);
         }
+        *reinterpret_cast<uint4*>(dst + ssd_swz(r, cpk)) = v;
       }
     }
   };
@@ -215,71 +290,32 @@ __global__ void __launch_bounds__(kSsdThreads, 2) ssd_chunk_scan(const SsdParams
                  src, ok);
     }
   };
-  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
-  auto unpack2 = [](uint32_t u) -> float2 {  // a 16-bit pair -> two floats
-    if constexpr (kBf16) {
-      return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
-    } else {
-      return __half22float2(*reinterpret_cast<const __half2*>(&u));
-    }
+  // Tensor-copy path: block j's x rows and cb rows -> buffers j % 3 (thread 0).
+  const int bcg = (b * p.NC + c) * p.G + g;
+  int armed[3] = {-1, -1, -1};  // thread 0: last block whose copies each buffer awaits
+  auto tma_blk = [&](int j) {
+    const int i = j % 3;
+    mbar_arrive_expect_tx(&bars->full[i],
+                          static_cast<uint32_t>(P * kSsdKBlk * 2 + kSsdRows * kSsdKBlk * 2));
+    for (int pc = 0; pc < P; pc += 64)
+      tma_load_4d(sm + L.x + i * L.x_stride + (pc >> 6) * (kSsdKBlk * 128), &tm_x,
+                  &bars->full[i], pc, h, c * Q + j * kSsdKBlk, b);
+    tma_load_3d(sm + L.wbuf(i), &tm_cb, &bars->full[i], j * kSsdKBlk, l0, bcg);
+    armed[i] = j;
   };
-  auto build_w = [&](int j) {  // W block j from cbr -> buffer j & 1
-    const int s0 = j * kSsdKBlk, sc = s0 + cpk * 8;
-    // exp(dA_l - dA_s) = exp(dA_l - ref) exp(ref - dA_s) with ref = dA[s0]
-    // when every exponent of the block (its keys, this tile's rows) stays
-    // within +-60 (both factors normal fp32 numbers); else per entry.
-    // (sdA is in log2 units: 60 / ln 2 = 86.56.)
-    const float ref = sdA[s0];
-    const float* rng = reinterpret_cast<const float*>(sm + L.rng);
-    const int r0 = l0 / kSsdKBlk, r1 = min(r0 + 1, (Q - 1) / kSsdKBlk);
-    const float lo = fminf(fminf(rng[j], rng[r0]), rng[r1]);
-    const float hi = fmaxf(fmaxf(rng[16 + j], rng[16 + r0]), rng[16 + r1]);
-    const bool fact = hi - ref <= 86.5f && ref - lo <= 86.5f;
-    float2 das[4], dts[4];  // key pairs of this thread's packet
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int s = sc + 2 * q;
-      das[q] = make_float2(s < Q ? sdA[s] : ref, s + 1 < Q ? sdA[s + 1] : ref);
-      dts[q] = make_float2(s < Q ? sdt[s] : 0.0f, s + 1 < Q ? sdt[s + 1] : 0.0f);
-      if (fact)  // exp(ref - dA_s) dt_s
-        dts[q] = fmul2(dts[q], make_float2(ex2(ref - das[q].x), ex2(ref - das[q].y)));
+  if constexpr (kTma) {
+    if (tid == 0) {
+      prefetch_tensormap(&tm_x);
+      prefetch_tensormap(&tm_c);
+      prefetch_tensormap(&tm_cb);
+      mbar_arrive_expect_tx(&bars->c_full, static_cast<uint32_t>(kSsdRows * N * 2));
+      for (int n0 = 0; n0 < N; n0 += 64)
+        tma_load_4d(sm + L.c + (n0 >> 6) * (kSsdRows * 128), &tm_c, &bars->c_full, n0, g,
+                    c * Q + l0, b);
+      tma_blk(0);
+      if (nblk > 1) tma_blk(1);
     }
-#pragma unroll
-    for (int it = 0; it < kSsdRows / kSsdRowGroups; ++it) {
-      const int r = rg + kSsdRowGroups * it;
-      const int l = l0 + r;
-      const uint32_t* cw = reinterpret_cast<const uint32_t*>(&cbr[it]);
-      const float dal = l < Q ? sdA[l] : ref;
-      // Rows whose whole packet is visible (l < Q, every key <= l) skip the mask.
-      const bool full = l < Q && sc + 7 <= l;
-      const float el = fact ? ex2(dal - ref) : 0.0f;
-      uint32_t pk[4];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        float2 e2;
-        if (fact) {
-          e2 = make_float2(el, el);
-        } else {
-          const float2 a = fadd2(make_float2(dal, dal), make_float2(-das[q].x, -das[q].y));
-          e2 = make_float2(ex2(a.x), ex2(a.y));
-        }
-        float2 w2 = fmul2(fmul2(unpack2(cw[q]), e2), dts[q]);
-        if (!full) {
-          const int s = sc + 2 * q;
-          w2.x = (l < Q && s <= l) ? w2.x : 0.0f;
-          w2.y = (l < Q && s + 1 <= l) ? w2.y : 0.0f;
-        }
-        pk[q] = pack16<T>(w2.x, w2.y);
-      }
-      *reinterpret_cast<uint4*>(sm + L.w + (j & 1) * (kSsdRows * 128) + ssd_swz(r, cpk)) =
-          make_uint4(pk[0], pk[1], pk[2], pk[3]);
-    }
-  };
-
-  // ---- prologue: x and C of block 0 (cp.async), cb rows of block 0 and prev
-  // (registers) all in flight together
-  issue_x(0);
-  {
+  } else {
     const T* Cg = static_cast<const T*>(p.C);
     const int upr = npad / 8;  // 16-byte units per row
     for (int i = tid; i < kSsdRows * upr; i += kSsdThreads) {
@@ -290,48 +326,59 @@ __global__ void __launch_bounds__(kSsdThreads, 2) ssd_chunk_scan(const SsdParams
                      (ok ? n : 0);
       cp_async16(sb + L.c + (n >> 6) * (kSsdRows * 128) + ssd_swz(r, (n & 63) >> 3), src, ok);
     }
-  }
-  cp_async_commit();  // group: x block 0 and the C tile
-  load_cb(0);
-  {
-    // prev (P x N fp32) -> dtype, K-major [p][n]; eight packets per thread
-    // loaded before any is converted.
-    const float* pg = p.prev + ((static_cast<int64_t>(b) * p.NC + c) * p.H + h) * P * N;
-    const int upr = npad / 8, total = P * upr;
-    for (int base = 0; base < total; base += 8 * kSsdThreads) {
-      float4 va[8], vb[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int i = base + k * kSsdThreads + tid;
-        va[k] = vb[k] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        if (i < total) {
-          const int r = static_cast<int>(p.div_c.div(i)), n = (i - r * upr) * 8;
-          if (n < N) {
-            const float* src = pg + static_cast<int64_t>(r) * N + n;
-            va[k] = __ldcs(reinterpret_cast<const float4*>(src));
-            vb[k] = __ldcs(reinterpret_cast<const float4*>(src + 4));
-          }
-        }
-      }
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int i = base + k * kSsdThreads + tid;
-        if (i < total) {
-          const int r = static_cast<int>(p.div_c.div(i)), n = (i - r * upr) * 8;
-          uint4 pk;
-          pk.x = pack16<T>(va[k].x, va[k].y);
-          pk.y = pack16<T>(va[k].z, va[k].w);
-          pk.z = pack16<T>(vb[k].x, vb[k].y);
-          pk.w = pack16<T>(vb[k].z, vb[k].w);
-          *reinterpret_cast<uint4*>(sm + L.prev + (n >> 6) * (P * 128) +
-                                    ssd_swz(r, (n & 63) >> 3)) = pk;
-        }
-      }
+    issue_x(0);
+    issue_cb(0);
+    cp_async_commit();  // group 0: the C tile, x and cb of block 0
+    if (nblk > 1) {
+      issue_x(1);
+      issue_cb(1);
+      cp_async_commit();  // group 1: x and cb of block 1
     }
   }
-  __syncthreads();  // sdA / sdt visible
+  // dA is kept in log2 units: exp(a - b) = ex2(a' - b').
+#pragma unroll
+  for (int k = 0; k < kMaxQPerThread; ++k) {
+    const int i = tid + k * kSsdThreads;
+    if (i < Q) {
+      sdA[i] = rdA[k] * 1.4426950408889634f;
+      sdt[i] = rdt[k];
+    }
+  }
+  store_prev(0);
+  for (int base = 8 * kSsdThreads; base < ptotal; base += 8 * kSsdThreads) {
+    load_prev(base);  // shapes with more than 8 prev packets per thread
+    store_prev(base);
+  }
+  if constexpr (!kTma) {
+    if (nblk > 1) cp_async_wait_prev();  // group 0 landed (this thread's copies)
+    else cp_async_wait_all();
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();  // C, prev, sdA / sdt, block 0 visible; barriers initialised
+  tc_fence_after();
+
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  const uint32_t id_kk = idesc_f16_major(kSsdRows, P, kBf16 ? 1 : 0, 0, 0);
+  const uint32_t id_kmn = idesc_f16_major(kSsdRows, P, kBf16 ? 1 : 0, 0, 1);
+  const uint32_t tmem = bars->tmem_base;
+  const uint32_t p64 = static_cast<uint32_t>((P + 63) & ~63);
+  const uint32_t t_d1 = tmem, t_d2 = tmem + p64;
+  bool ok = true;
+  if (tid == 0) {  // history: D1 = C prev^T
+    if constexpr (kTma) ok = mbar_wait(&bars->c_full, 0, p.err, abort_flag);
+    const uint64_t a = smem_desc(sb + L.c, 16, 1024);
+    const uint64_t bd = smem_desc(sb + L.prev, 16, 1024);
+    if (ok) {
+      tc_fence_after();
+      for (int kk = 0; kk < npad / 16; ++kk)
+        mma_f16_ss(t_d1, desc_advance(a, (kk >> 2) * (kSsdRows * 128) + (kk & 3) * 32),
+                   desc_advance(bd, (kk >> 2) * (P * 128) + (kk & 3) * 32), id_kk, kk > 0);
+    }
+    mma_commit(&bars->d1_done);
+  }
   {
-    // min / max of dA over each 64-key block (warp w: blocks w, w + 4, ...)
+    // min / max of dA over each 64-key block (warp w: blocks w, w + 8, ...)
     float* rng = reinterpret_cast<float*>(sm + L.rng);
     const int lane = tid & 31;
     for (int jb = warp; jb * kSsdKBlk < Q; jb += kSsdThreads / 32) {
@@ -356,49 +403,155 @@ __global__ void __launch_bounds__(kSsdThreads, 2) ssd_chunk_scan(const SsdParams
   }
   __syncthreads();
 
-  const uint32_t id_kk = idesc_f16_major(kSsdRows, P, kBf16 ? 1 : 0, 0, 0);
-  const uint32_t id_kmn = idesc_f16_major(kSsdRows, P, kBf16 ? 1 : 0, 0, 1);
-  const uint32_t tmem = bars->tmem_base;
-  const uint32_t p64 = static_cast<uint32_t>((P + 63) & ~63);
-  const uint32_t t_d1 = tmem, t_d2 = tmem + p64;
-  bool ok = true;
-  int issued = 0;  // key blocks whose MMAs were issued
-  for (int j = 0; j < nblk; ++j) {
-    const int buf = j & 1;
-    if (j >= 2) {
-      // Block j - 2's MMAs read W buffer `buf` and x buffer (j + 1) % 3.
-      if (!mbar_wait(&bars->blk_done[buf], ((j - 2) >> 1) & 1, p.err, abort_flag)) ok = false;
-      if (!__syncthreads_and(ok)) {
-        ok = false;
-        break;
+  auto unpack2 = [](uint32_t u) -> float2 {  // a 16-bit pair -> two floats
+    if constexpr (kBf16) {
+      return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
+    } else {
+      return __half22float2(*reinterpret_cast<const __half2*>(&u));
+    }
+  };
+  auto build_w = [&](int j) {  // cb block j -> W, in place in buffer j % 3
+    const int s0 = j * kSsdKBlk, sc = s0 + cpk * 8;
+    uint8_t* wb = sm + L.wbuf(j % 3);
+    // exp(dA_l - dA_s) = exp(dA_l - ref) exp(ref - dA_s) with ref = dA[s0]
+    // when neither factor can overflow: the block's keys lie within 2^100 of
+    // ref (ref - min dA_s <= 100 in log2 units) and no row of the tile lies
+    // more than 2^100 above it.  A row factor that underflows belongs to an
+    // entry whose true decay exp(dA_l - dA_s) is below 2^(100-126), which is
+    // invisible next to the 16-bit W of the row's own keys.  Else per entry.
+    const float ref = sdA[s0];
+    const float* rng = reinterpret_cast<const float*>(sm + L.rng);
+    const int r0 = l0 / kSsdKBlk, r1 = min(r0 + 1, (Q - 1) / kSsdKBlk);
+    const float hi_rows = fmaxf(rng[16 + r0], rng[16 + r1]);
+    const bool fact = ref - rng[j] <= 100.0f && hi_rows - ref <= 100.0f;
+    float2 das[4], dts[4];  // key pairs of this thread's packet
+    if (sc + 8 <= Q) {  // 32-byte aligned: sc is a multiple of 8
+      const float4 a0 = *reinterpret_cast<const float4*>(sdA + sc);
+      const float4 a1 = *reinterpret_cast<const float4*>(sdA + sc + 4);
+      const float4 t0 = *reinterpret_cast<const float4*>(sdt + sc);
+      const float4 t1 = *reinterpret_cast<const float4*>(sdt + sc + 4);
+      das[0] = make_float2(a0.x, a0.y);
+      das[1] = make_float2(a0.z, a0.w);
+      das[2] = make_float2(a1.x, a1.y);
+      das[3] = make_float2(a1.z, a1.w);
+      dts[0] = make_float2(t0.x, t0.y);
+      dts[1] = make_float2(t0.z, t0.w);
+      dts[2] = make_float2(t1.x, t1.y);
+      dts[3] = make_float2(t1.z, t1.w);
+    } else {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int s = sc + 2 * q;
+        das[q] = make_float2(s < Q ? sdA[s] : ref, s + 1 < Q ? sdA[s + 1] : ref);
+        dts[q] = make_float2(s < Q ? sdt[s] : 0.0f, s + 1 < Q ? sdt[s + 1] : 0.0f);
       }
     }
-    if (j + 1 < nblk) issue_x(j + 1);  // one block ahead
-    cp_async_commit();
-    build_w(j);
-    if (j + 1 < nblk) load_cb(j + 1);  // in flight during this block's MMAs
-    cp_async_wait_prev();              // x of block j (and the C tile) landed
+    if (fact) {  // exp(ref - dA_s) dt_s
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        dts[q] = fmul2(dts[q], make_float2(ex2(ref - das[q].x), ex2(ref - das[q].y)));
+    }
+#pragma unroll
+    for (int it = 0; it < kSsdRows / kSsdRowGroups; ++it) {
+      const int r = rg + kSsdRowGroups * it;
+      const int l = l0 + r;
+      uint4* slot = reinterpret_cast<uint4*>(wb + ssd_swz(r, cpk));
+      // Packets wholly above the diagonal or past the chunk are zero.
+      if (!(l < Q && sc <= l && sc < Q)) {
+        *slot = make_uint4(0u, 0u, 0u, 0u);
+        continue;
+      }
+      const uint4 cbv = *slot;
+      const uint32_t* cw = reinterpret_cast<const uint32_t*>(&cbv);
+      const float dal = sdA[l];
+      // Rows whose whole packet is visible (every key <= l, < Q) skip the mask.
+      const bool full = sc + 7 <= l && sc + 8 <= Q;
+      const float el = fact ? ex2(dal - ref) : 0.0f;
+      uint32_t pk[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float2 e2;
+        if (fact) {
+          e2 = make_float2(el, el);
+        } else {
+          const float2 a = fadd2(make_float2(dal, dal), make_float2(-das[q].x, -das[q].y));
+          e2 = make_float2(ex2(a.x), ex2(a.y));
+        }
+        float2 w2 = fmul2(fmul2(unpack2(cw[q]), e2), dts[q]);
+        if (!full) {
+          const int s = sc + 2 * q;
+          w2.x = (s <= l && s < Q) ? w2.x : 0.0f;
+          w2.y = (s + 1 <= l && s + 1 < Q) ? w2.y : 0.0f;
+        }
+        pk[q] = pack16<T>(w2.x, w2.y);
+      }
+      *slot = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    }
+  };
+
+  int issued = 0;  // key blocks whose MMAs were issued
+  for (int j = 0; j < nblk; ++j) {
+    // cb and x of block j landed.
+    bool okj = true;
+    if constexpr (kTma) {
+      okj = mbar_wait(&bars->full[j % 3], (j / 3) & 1, p.err, abort_flag);
+    } else if (j > 0) {  // group j: all but the groups committed after it
+      if (j + 1 < nblk) cp_async_wait_prev();
+      else cp_async_wait_all();
+    }
+    if (okj) build_w(j);
     fence_proxy_async_smem();
     tc_fence_before();
-    __syncthreads();
+    // Uniform: every thread leaves the loop here or none does.
+    if (!__syncthreads_and(okj && ok)) {
+      ok = false;
+      break;
+    }
     tc_fence_after();
     if (tid == 0) {
-      if (j == 0) {
-        const uint64_t a = smem_desc(sb + L.c, 16, 1024);
-        const uint64_t bd = smem_desc(sb + L.prev, 16, 1024);
-        for (int kk = 0; kk < npad / 16; ++kk)
-          mma_f16_ss(t_d1, desc_advance(a, (kk >> 2) * (kSsdRows * 128) + (kk & 3) * 32),
-                     desc_advance(bd, (kk >> 2) * (P * 128) + (kk & 3) * 32), id_kk, kk > 0);
-      }
-      const uint64_t a = smem_desc(sb + L.w + buf * (kSsdRows * 128), 16, 1024);
+      const uint64_t a = smem_desc(sb + L.wbuf(j % 3), 16, 1024);
       const uint64_t bd = smem_desc(sb + L.x + (j % 3) * L.x_stride, kSsdKBlk * 128, 1024);
 #pragma unroll
       for (int kk = 0; kk < kSsdKBlk / 16; ++kk)
         mma_f16_ss(t_d2, desc_advance(a, kk * 32), desc_advance(bd, kk * 16 * 128), id_kmn,
                    (j > 0 || kk > 0) ? 1u : 0u);
-      mma_commit(&bars->blk_done[buf]);
+      mma_commit(&bars->blk_done[j % 3]);
     }
     issued = j + 1;
+    if (j + 2 < nblk) {
+      // Block j + 2 goes to the buffers block j - 1 read (for j = 0: the
+      // third cb buffer, the C tile, which the history MMA read).
+      if constexpr (kTma) {
+        if (tid == 0) {
+          // A failed wait shows at the next iteration's barrier, before any
+          // thread waits for the block not issued here.
+          ok = j >= 1 ? mbar_wait(&bars->blk_done[(j - 1) % 3], ((j - 1) / 3) & 1, p.err,
+                                  abort_flag)
+                      : mbar_wait(&bars->d1_done, 0, p.err, abort_flag);
+          if (ok) tma_blk(j + 2);
+        }
+      } else {
+        bool free_ok = j >= 1 ? mbar_wait(&bars->blk_done[(j - 1) % 3], ((j - 1) / 3) & 1,
+                                          p.err, abort_flag)
+                              : mbar_wait(&bars->d1_done, 0, p.err, abort_flag);
+        if (!__syncthreads_and(free_ok)) {
+          ok = false;
+          break;
+        }
+        issue_x(j + 2);
+        issue_cb(j + 2);
+        cp_async_commit();
+      }
+    }
+  }
+  if constexpr (kTma) {
+    // No tensor copy may still write this CTA's shared memory at exit: the
+    // last block each buffer was armed for, and the C tile.
+    if (tid == 0) {
+      mbar_wait(&bars->c_full, 0, p.err, abort_flag, true);
+      for (int i = 0; i < 3; ++i)
+        if (armed[i] >= 0) mbar_wait(&bars->full[i], (armed[i] / 3) & 1, p.err, abort_flag, true);
+    }
   }
   cp_async_wait_all();  // no copy may still write this CTA's shared memory at exit
   if (tid == 0) mma_commit(&bars->all_done);
@@ -418,6 +571,35 @@ __global__ void __launch_bounds__(kSsdThreads, 2) ssd_chunk_scan(const SsdParams
     const uint32_t lane = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const float eh = l < Q ? ex2(sdA[l]) : 0.0f;
     const int U = P / 4;                            // units per row
+    if (kTma && Q % kSsdRows == 0) {
+      // Staged as 32-column (128-byte) slabs [128 rows][32] fp32 with the
+      // 128-byte swizzle (16-byte unit u of row r at u ^ (r % 8)), each slab
+      // written by one tensor store.
+      uint8_t* stg = sm + L.w;
+      for (int c0 = 32 * (warp >> 2); c0 < P; c0 += 64) {
+        uint32_t x1[32], x2[32];
+        tmem_ld32(t_d1 + lane + c0, x1);
+        tmem_ld32(t_d2 + lane + c0, x2);
+        tmem_wait_ld_regs(x1);
+        tmem_wait_ld_regs(x2);
+        uint8_t* slab = stg + (c0 >> 5) * (kSsdRows * 128) + r * 128;
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          *reinterpret_cast<float4*>(slab + ((u ^ (r & 7)) << 4)) =
+              make_float4(fmaf(eh, __uint_as_float(x1[4 * u]), __uint_as_float(x2[4 * u])),
+                          fmaf(eh, __uint_as_float(x1[4 * u + 1]), __uint_as_float(x2[4 * u + 1])),
+                          fmaf(eh, __uint_as_float(x1[4 * u + 2]), __uint_as_float(x2[4 * u + 2])),
+                          fmaf(eh, __uint_as_float(x1[4 * u + 3]), __uint_as_float(x2[4 * u + 3])));
+      }
+      fence_proxy_async_smem();
+      __syncthreads();
+      if (tid == 0) {
+        for (int c0 = 0; c0 < P; c0 += 32)
+          tma_store_4d(&tm_out, stg + (c0 >> 5) * (kSsdRows * 128), c0, h, c * Q + l0, b);
+        bulk_commit();
+        bulk_wait_read_all();  // the staging tile is read before the CTA exits
+      }
+    } else {
     const int smask = (U & 7) == 0 ? 7 : 3;
     float* stg = reinterpret_cast<float*>(sm + L.w);
     for (int c0 = 32 * (warp >> 2); c0 < P; c0 += 64) {
@@ -447,6 +629,7 @@ __global__ void __launch_bounds__(kSsdThreads, 2) ssd_chunk_scan(const SsdParams
                  p.out + ((static_cast<int64_t>(b) * S + c * Q + l0 + rr) * p.H + h) * P + u * 4),
              v);
     }
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -458,13 +641,47 @@ __global__ void __launch_bounds__(kSsdThreads, 2) ssd_chunk_scan(const SsdParams
 
 template <typename T>
 int launch_ssd(const SsdParams& p, cudaStream_t s) {
-  auto k = ssd_chunk_scan<T>;
+  constexpr bool bf16 = std::is_same<T, __nv_bfloat16>::value;
+  // Tensor copies need whole 64-element boxes of x / C columns and whole
+  // 64-key blocks of the chunk (a block never crosses into the next chunk).
+  CUtensorMap tm_x, tm_c, tm_cb, tm_out;
+  memset(&tm_x, 0, sizeof(tm_x));
+  memset(&tm_c, 0, sizeof(tm_c));
+  memset(&tm_cb, 0, sizeof(tm_cb));
+  memset(&tm_out, 0, sizeof(tm_out));
+  bool tma = p.Q % 64 == 0 && p.P % 64 == 0 && p.N % 64 == 0;
+  if (tma) {
+    const int S = p.NC * p.Q;
+    const uint64_t cb_dims[3] = {static_cast<uint64_t>(p.Q), static_cast<uint64_t>(p.Q),
+                                 static_cast<uint64_t>(p.B) * p.NC * p.G};
+    const uint64_t cb_strides[2] = {static_cast<uint64_t>(p.Q) * 2,
+                                    static_cast<uint64_t>(p.Q) * p.Q * 2};
+    const uint32_t cb_box[3] = {64, static_cast<uint32_t>(kSsdRows), 1};
+    tma = make_bshd_map(&tm_x, p.x, p.P, p.H, S, p.B, kSsdKBlk, bf16) &&
+          make_bshd_map(&tm_c, p.C, p.N, p.G, S, p.B, kSsdRows, bf16) &&
+          make_tiled_map_16bit(&tm_cb, p.cb, bf16, 3, cb_dims, cb_strides, cb_box);
+    if (tma && p.Q % kSsdRows == 0) {  // out (B, S, H, P) fp32: box (32, 1, 128, 1)
+      auto fn = tensor_map_encoder();
+      const cuuint64_t dims[4] = {static_cast<cuuint64_t>(p.P), static_cast<cuuint64_t>(p.H),
+                                  static_cast<cuuint64_t>(S), static_cast<cuuint64_t>(p.B)};
+      const cuuint64_t strides[3] = {static_cast<cuuint64_t>(p.P) * 4,
+                                     static_cast<cuuint64_t>(p.P) * p.H * 4,
+                                     static_cast<cuuint64_t>(p.P) * p.H * S * 4};
+      const cuuint32_t box[4] = {32, 1, static_cast<cuuint32_t>(kSsdRows), 1};
+      const cuuint32_t estride[4] = {1, 1, 1, 1};
+      tma = fn && fn(&tm_out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, p.out, dims, strides, box,
+                     estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    }
+  }
+  auto k = tma ? ssd_chunk_scan<T, true> : ssd_chunk_scan<T, false>;
   const int smem = SsdLayout(p.P, p.N, p.Q).bytes + 1024;  // + room to align the base
   if (smem > 232448) return TILEOPS_EBADSHAPE;
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return TILEOPS_ELAUNCH;
   const int64_t grid = static_cast<int64_t>(p.B) * p.NC * p.H * p.ltiles;
-  k<<<static_cast<unsigned>(grid), kSsdThreads, smem, s>>>(p);
+  k<<<static_cast<unsigned>(grid), kSsdThreads, smem, s>>>(p, tm_x, tm_c, tm_cb, tm_out);
   return launch_status();
 }
 
