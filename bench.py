@@ -887,7 +887,7 @@ def time_sharded_steps(wl: Workload, op, sets: list, steps: int, warmup: int, wo
             "parts_per_rank": parts}
 
 
-def time_e2e(wl: Workload, host_full: tuple, device, steps: int, max_chunks: int = 16,
+def time_e2e(wl: Workload, host_full: tuple, device, steps: int, max_chunks: int = 4,
              copy_streams: int = 1) -> dict:
     """The public op API from pinned host buffers, chunked so that copies in
     both directions overlap the kernels: per chunk, H2D on an input stream,
@@ -1290,8 +1290,10 @@ def main() -> None:
                          "baseline already)")
     ap.add_argument("--per-op-steps", type=int, default=20,
                     help="timed calls per op in per_op (the headline uses --steps)")
-    ap.add_argument("--e2e-chunks", type=int, default=16,
-                    help="chunks per step in the end-to-end leg (at most)")
+    ap.add_argument("--e2e-chunks", type=int, default=4,
+                    help="chunks per step in the end-to-end leg (at most; 4 measured "
+                         "fastest: each chunk costs ~0.1 ms of host time for the op call "
+                         "and its copies)")
     ap.add_argument("--pieces", type=int, default=1,
                     help="N > 1: parts per rank; each part's outputs are gathered while the "
                          "next part computes (1 = one shard per rank, gathered after it; "
