@@ -577,12 +577,13 @@ __global__ void __launch_bounds__(128, 4)
   __syncthreads();
 
   // ---- Wk = Tk K (C x DK), then (once V has landed) U = Tv V (C x DV): warp
-  // w owns rows 16w..16w+15; T is lower triangular, so k-blocks 0..w.  Each
+  // w owns output columns [w D/4, (w+1) D/4) of all four 16-row blocks; T is
+  // lower triangular, so row block m takes k-blocks 0..m (every warp the same
+  // ten (m, k) pairs: the work is balanced across the warps).  Each
   // result is staged in shared memory (swizzled [64][64] boxes, the freed K
   // tile for -Wk, the freed Tk / Tv tile for U) and written by TMA stores, so
   // the workspace sees whole 128-byte lines.
   {
-    const int m0 = warp * 16;
 #pragma unroll
     for (int which = 0; which < 2; ++which) {
       if (which == 1) {
@@ -601,25 +602,31 @@ __global__ void __launch_bounds__(128, 4)
         }
       }
       constexpr int kMaxD = DK > DV ? DK : DV;
+      constexpr int kMaxNT = kMaxD / 32;  // 8-column tiles per warp
       const int D = which == 0 ? DK : DV;
+      const int NT = D / 32;
+      const int cw = warp * NT * 8;  // first output column of this warp
       const uint32_t tA = sb + L::kQs + which * 8192;
       const uint32_t X = which == 0 ? sK : sV;
-      float acc[kMaxD / 64][8][4];
+      float acc[4][kMaxNT][4];
 #pragma unroll
-      for (int nb = 0; nb < kMaxD / 64; ++nb) {
-        if (nb * 64 >= D) break;
+      for (int m = 0; m < 4; ++m)
 #pragma unroll
-        for (int n = 0; n < 8; ++n)
-          acc[nb][n][0] = acc[nb][n][1] = acc[nb][n][2] = acc[nb][n][3] = 0.0f;
-        for (int kk = 0; kk <= warp; ++kk) {
+        for (int n = 0; n < kMaxNT; ++n)
+          acc[m][n][0] = acc[m][n][1] = acc[m][n][2] = acc[m][n][3] = 0.0f;
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+#pragma unroll
+        for (int kk = 0; kk <= m; ++kk) {
           uint32_t a[4];
-          sfrag_a(a, tA, m0, kk * 16);
+          sfrag_a(a, tA, m * 16, kk * 16);
 #pragma unroll
-          for (int n = 0; n < 8; n += 2) {
+          for (int n = 0; n < kMaxNT; n += 2) {
+            if (n >= NT) break;
             uint32_t bb[4];
-            sfrag_b_kn(bb, X, kk * 16, nb * 64 + n * 8);
-            mma_bf16(acc[nb][n], a, bb[0], bb[1]);
-            mma_bf16(acc[nb][n + 1], a, bb[2], bb[3]);
+            sfrag_b_kn(bb, X, kk * 16, cw + n * 8);
+            mma_bf16(acc[m][n], a, bb[0], bb[1]);
+            mma_bf16(acc[m][n + 1], a, bb[2], bb[3]);
           }
         }
       }
@@ -628,16 +635,15 @@ __global__ void __launch_bounds__(128, 4)
       uint8_t* stage = sm + (which == 0 ? L::kKs : L::kQs);
       const float sg = which == 0 ? -1.0f : 1.0f;
 #pragma unroll
-      for (int nb = 0; nb < kMaxD / 64; ++nb) {
-        if (nb * 64 >= D) break;
+      for (int m = 0; m < 4; ++m) {
 #pragma unroll
-        for (int n = 0; n < 8; ++n) {
-          const int l = m0 + g8, c0 = n * 8;  // 8-column unit within the 64-wide box
-          uint8_t* box = stage + nb * 8192;
-          *reinterpret_cast<uint32_t*>(box + swz(l, c0) + t2 * 2) =
-              pack_bf16(sg * acc[nb][n][0], sg * acc[nb][n][1]);
-          *reinterpret_cast<uint32_t*>(box + swz(l + 8, c0) + t2 * 2) =
-              pack_bf16(sg * acc[nb][n][2], sg * acc[nb][n][3]);
+        for (int n = 0; n < kMaxNT; ++n) {
+          if (n >= NT) break;
+          const int l = m * 16 + g8, col = cw + n * 8;  // swz() adds the 64-column box
+          *reinterpret_cast<uint32_t*>(stage + swz(l, col) + t2 * 2) =
+              pack_bf16(sg * acc[m][n][0], sg * acc[m][n][1]);
+          *reinterpret_cast<uint32_t*>(stage + swz(l + 8, col) + t2 * 2) =
+              pack_bf16(sg * acc[m][n][2], sg * acc[m][n][3]);
         }
       }
       sm100::fence_proxy_async_smem();
