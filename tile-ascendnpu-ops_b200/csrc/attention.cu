@@ -318,11 +318,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       float mx[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) mx[i] = -INFINITY;
-      if (!need_mask) {
+      if (!need_mask) {  // two scores per three-input max
 #pragma unroll
         for (int c = 0; c < kBN / 32; ++c)
 #pragma unroll
-          for (int i = 0; i < 32; ++i) mx[i & 7] = fmaxf(mx[i & 7], __uint_as_float(sc[c][i]));
+          for (int i = 0; i < 16; ++i)
+            mx[i & 7] = fmax3(mx[i & 7], __uint_as_float(sc[c][2 * i]),
+                              __uint_as_float(sc[c][2 * i + 1]));
       } else {
 #pragma unroll
         for (int c = 0; c < kBN / 32; ++c)

@@ -18,13 +18,17 @@
 //   D1 = C_tile [128 x N] . prev^T        A K-major (C rows), B K-major (prev
 //                                          rows p, converted fp32 -> dtype)
 //   D2 = W [128 x s] . x [s x P]          A = W built per 64-key block in
-//                                          registers, B MN-major (x rows s)
+//                                          shared memory, B MN-major (x rows s)
 // with W[l, s] = cb[l, s] exp(dA[l] - dA[s]) dt[s] for s <= l (< Q), else 0.
-// Operands are staged with cp.async (16-byte copies, zero fill past the
-// chunk / past N) into 128-byte-swizzled shared tiles; W blocks are double-
-// and x blocks triple-buffered: the x rows of block j+1 are requested while
-// block j's W is built and its MMAs run.
-// Epilogue: out = exp(dA[l]) D1 + D2 straight from TMEM to global fp32.
+// The cb rows of a key block land in shared memory and are turned into W in
+// place; cb / W and x blocks are triple-buffered (the third cb / W buffer is
+// the C tile once the history MMA has read it) and requested two blocks
+// ahead.  Loads: with chunk length, d_head and d_state multiples of 64 the C
+// tile, x and cb blocks are tensor copies (one thread, mbarrier completion),
+// otherwise 16-byte cp.async from every thread (zero fill past the chunk /
+// past N).  Epilogue: out = exp(dA[l]) D1 + D2 from TMEM, staged in shared
+// memory and written by tensor stores (chunk length a multiple of 128) or by
+// row-wise vector stores.
 // Every mbarrier wait is bounded (2 s); a timeout sets the device error flag,
 // the MMAs issued so far are drained and TMEM is freed before returning.
 #include <cudaTypedefs.h>
