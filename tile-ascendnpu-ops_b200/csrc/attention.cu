@@ -39,9 +39,11 @@
 // in log2 units, so P <= 256 and rescales are rare; exp2 is ex2.approx on
 // exp2(scale*log2e*s - m), the FMA and the row sum as packed f32x2
 // instructions; P is stored 32 scores at a time.
-// Every mbarrier wait is bounded (2 s): on timeout the kernel records an
-// error (tileops_device_error_flag), drains its copies / MMAs, frees TMEM and
-// returns.
+// Every mbarrier wait (sm100::mbar_wait) checks a 2 s limit between its
+// try_wait polls: a phase that completes late ends the wait with an error
+// (tileops_device_error_flag), and the kernel drains its copies / MMAs, frees
+// TMEM and returns.  (A phase that never completes can park try_wait beyond
+// the limit; none exists in this pipeline.)
 #include <cudaTypedefs.h>
 
 #include <mutex>

@@ -29,8 +29,9 @@
 // past N).  Epilogue: out = exp(dA[l]) D1 + D2 from TMEM, staged in shared
 // memory and written by tensor stores (chunk length a multiple of 128) or by
 // row-wise vector stores.
-// Every mbarrier wait is bounded (2 s); a timeout sets the device error flag,
-// the MMAs issued so far are drained and TMEM is freed before returning.
+// Every mbarrier wait (sm100::mbar_wait) checks a 2 s limit between its
+// try_wait polls; a phase that completes late sets the device error flag, the
+// MMAs issued so far are drained and TMEM is freed before returning.
 #include <cudaTypedefs.h>
 
 #include <type_traits>
