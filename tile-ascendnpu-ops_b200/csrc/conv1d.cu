@@ -287,6 +287,7 @@ struct IgParams {
   bool w_vec;       // W rows are 16-byte multiples and aligned: cp.async path
   bool x_win;       // stride 1 and x 16-byte aligned: windowed 16-byte gather
   bool y_pair;      // rows of y start 4-byte aligned: paired stores in the epilogue
+  bool y_vec;       // rows of y start 16-byte aligned: 16-byte stores in the epilogue
   FastDivU32 div_k;
   int* err;
 };
@@ -311,8 +312,10 @@ __device__ __forceinline__ uint4 ig_window(const uint4& a, const uint4& b, int m
   }
 }
 
+// Three CTAs per SM: shared memory (two 32 KB stages each) allows three, and
+// the register cap keeps the batched gather loads from halving that.
 template <typename T>
-__global__ void __launch_bounds__(kIgThreads) conv1d_igemm(const IgParams p) {
+__global__ void __launch_bounds__(kIgThreads, 3) conv1d_igemm(const IgParams p) {
   using namespace sm100;
   extern __shared__ uint8_t ig_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>(
@@ -398,23 +401,43 @@ __global__ void __launch_bounds__(kIgThreads) conv1d_igemm(const IgParams p) {
       // thread -> 16-byte units i = tid + 256 q (row i / 16, positions
       // 8 (i % 16)..), each from two aligned 16-byte loads and a funnel shift;
       // units that cross a row edge or the end of x go element by element.
+      // Every unit's aligned loads are issued before the first shared-memory
+      // store (a store may not be reordered above a later generic load, so
+      // loads interleaved with stores would cost one round trip per unit).
+      constexpr int kUnits = kIgK * kIgN / 8 / kIgThreads;
+      uint4 lo[kUnits], hi[kUnits];
+      int mm[kUnits];
+      bool fast[kUnits];
 #pragma unroll
-      for (int q = 0; q < kIgK * kIgN / 8 / kIgThreads; ++q) {
+      for (int q = 0; q < kUnits; ++q) {
         const int i = tid + q * kIgThreads;
         const int rr = i >> 4, u = i & 15;
         const int64_t coff = tb[2 * rr];
         const int64_t pos = static_cast<int64_t>(o0) - p.pad_left + tb[2 * rr + 1] + u * 8;
+        const uintptr_t src =
+            reinterpret_cast<uintptr_t>(xg) + static_cast<uintptr_t>(coff + pos) * sizeof(T);
+        const uintptr_t a16 = src & ~static_cast<uintptr_t>(15);
+        mm[q] = static_cast<int>((src - a16) >> 1);
+        fast[q] = coff >= 0 && pos >= 0 && pos + 8 <= p.l_in &&
+                  a16 + 32 <= reinterpret_cast<uintptr_t>(p.x_end);
+        lo[q] = hi[q] = make_uint4(0u, 0u, 0u, 0u);
+        if (fast[q]) {
+          lo[q] = *reinterpret_cast<const uint4*>(a16);
+          if (mm[q]) hi[q] = *reinterpret_cast<const uint4*>(a16 + 16);
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < kUnits; ++q) {
+        const int i = tid + q * kIgThreads;
+        const int rr = i >> 4, u = i & 15;
         uint4 val = make_uint4(0u, 0u, 0u, 0u);
-        if (coff >= 0) {
-          const T* src = xg + coff + pos;
-          const uintptr_t a16 = reinterpret_cast<uintptr_t>(src) & ~static_cast<uintptr_t>(15);
-          const int m = static_cast<int>((reinterpret_cast<uintptr_t>(src) - a16) >> 1);
-          if (pos >= 0 && pos + 8 <= p.l_in &&
-              a16 + 32 <= reinterpret_cast<uintptr_t>(p.x_end)) {
-            const uint4 lo = *reinterpret_cast<const uint4*>(a16);
-            const uint4 hi = m ? *reinterpret_cast<const uint4*>(a16 + 16) : lo;
-            val = ig_window(lo, hi, m);
-          } else {
+        if (fast[q]) {
+          val = ig_window(lo[q], mm[q] ? hi[q] : lo[q], mm[q]);
+        } else {
+          const int64_t coff = tb[2 * rr];
+          if (coff >= 0) {
+            const int64_t pos = static_cast<int64_t>(o0) - p.pad_left + tb[2 * rr + 1] + u * 8;
+            const T* src = xg + coff + pos;
             T* e = reinterpret_cast<T*>(&val);
 #pragma unroll
             for (int j = 0; j < 8; ++j)
@@ -549,25 +572,36 @@ __global__ void __launch_bounds__(kIgThreads) conv1d_igemm(const IgParams p) {
     // (y aligned, l_out and o0 even): lane l writes columns 2l, 2l + 1,
     // 2l + 64, 2l + 65 of its warp's rows; otherwise single elements.
     const bool pairs = p.y_pair && (ncol & 1) == 0;
-    for (int rr = warp; rr < nrow; rr += kIgThreads / 32) {
-      T* yr = ybase + static_cast<int64_t>(rr) * p.l_out;
-      const uint8_t* sr = stg + rr * 256;
-      if (pairs) {
+    if (p.y_vec) {
+      // 16-byte units: half-warp per row, two rows per warp instruction
+      // (ncol is a multiple of 8 here since l_out and o0 are).
+      const int u = tid & 15;
+      for (int rr = 2 * warp + ((tid >> 4) & 1); rr < nrow; rr += kIgThreads / 16) {
+        if (u * 8 < ncol)
+          *reinterpret_cast<uint4*>(ybase + static_cast<int64_t>(rr) * p.l_out + u * 8) =
+              *reinterpret_cast<const uint4*>(stg + rr * 256 + ((u ^ (rr & 15)) << 4));
+      }
+    } else {
+      for (int rr = warp; rr < nrow; rr += kIgThreads / 32) {
+        T* yr = ybase + static_cast<int64_t>(rr) * p.l_out;
+        const uint8_t* sr = stg + rr * 256;
+        if (pairs) {
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int c = 2 * (tid & 31) + 64 * h;
-          if (c < ncol) {
-            const uint32_t v =
-                *reinterpret_cast<const uint32_t*>(sr + (((c >> 3) ^ (rr & 15)) << 4) + (c & 7) * 2);
-            *reinterpret_cast<uint32_t*>(yr + c) = v;
+          for (int h = 0; h < 2; ++h) {
+            const int c = 2 * (tid & 31) + 64 * h;
+            if (c < ncol) {
+              const uint32_t v =
+                  *reinterpret_cast<const uint32_t*>(sr + (((c >> 3) ^ (rr & 15)) << 4) + (c & 7) * 2);
+              *reinterpret_cast<uint32_t*>(yr + c) = v;
+            }
           }
-        }
-      } else {
+        } else {
 #pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          const int c = (tid & 31) + 32 * h;
-          if (c < ncol)
-            yr[c] = *reinterpret_cast<const T*>(sr + (((c >> 3) ^ (rr & 15)) << 4) + (c & 7) * 2);
+          for (int h = 0; h < 4; ++h) {
+            const int c = (tid & 31) + 32 * h;
+            if (c < ncol)
+              yr[c] = *reinterpret_cast<const T*>(sr + (((c >> 3) ^ (rr & 15)) << 4) + (c & 7) * 2);
+          }
         }
       }
     }
@@ -605,6 +639,7 @@ int launch_igemm(const void* x, const void* w, const void* bias, void* y, int64_
   p.w_vec = p.R % 8 == 0 && aligned16(w);
   p.x_win = stride == 1 && aligned16(x);
   p.y_pair = (reinterpret_cast<uintptr_t>(y) & 3u) == 0 && l_out % 2 == 0;
+  p.y_vec = aligned16(y) && l_out % 8 == 0;
   p.div_k = FastDivU32(static_cast<uint32_t>(K));
   p.err = device_error_ptr();
   auto k = conv1d_igemm<T>;
