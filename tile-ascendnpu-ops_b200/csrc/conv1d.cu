@@ -372,20 +372,20 @@ __global__ void __launch_bounds__(kIgThreads, 3) conv1d_igemm(const IgParams p) 
                      : "memory");
       }
     } else {
-      // Element path: loads in batches of 8 in flight before their stores.
-      constexpr int kPer = kIgM * kIgK / kIgThreads;
+      // Element path: loads in batches of 16 in flight before their stores.
+      constexpr int kPer = kIgM * kIgK / kIgThreads, kBatch = 16;
 #pragma unroll 1
-      for (int q0 = 0; q0 < kPer; q0 += 8) {
-        T v[8];
+      for (int q0 = 0; q0 < kPer; q0 += kBatch) {
+        T v[kBatch];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
+        for (int q = 0; q < kBatch; ++q) {
           const int i = tid + (q0 + q) * kIgThreads;
           const int row = i >> 6, r = r0 + (i & 63);
           v[q] = (co0 + row < p.cog && r < p.R) ? wg[static_cast<int64_t>(row) * p.R + r]
                                                 : Cvt<T>::from_f(0.0f);
         }
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
+        for (int q = 0; q < kBatch; ++q) {
           const int i = tid + (q0 + q) * kIgThreads;
           const int row = i >> 6, col = i & 63;
           *reinterpret_cast<T*>(st + ig_swz(row, col >> 3) + (col & 7) * 2) = v[q];
