@@ -894,6 +894,10 @@ def time_e2e(wl: Workload, host_full: tuple, device, steps: int, max_chunks: int
     the op on the compute stream, D2H of its outputs on an output stream
     (``copy_streams`` streams each way, chunks dealt round-robin).  Returns ms
     per step (all chunks) and the bytes copied each way."""
+    # A chunk costs ~0.1 ms of host time (op call, copies, events): no chunk
+    # gets less than 4 MB of input.
+    in_bytes = sum(t.numel() * t.element_size() for t in host_full if isinstance(t, torch.Tensor))
+    max_chunks = max(1, min(max_chunks, in_bytes // (4 << 20)))
     n_chunks = 1
     for c in (max_chunks, 16, 8, 4, 2):
         if c <= max_chunks and wl.shard is not None and wl.shard(host_full, 0, c) is not None:
@@ -1293,7 +1297,7 @@ def main() -> None:
     ap.add_argument("--e2e-chunks", type=int, default=4,
                     help="chunks per step in the end-to-end leg (at most; 4 measured "
                          "fastest: each chunk costs ~0.1 ms of host time for the op call "
-                         "and its copies)")
+                         "and its copies; no chunk gets less than 4 MB of input)")
     ap.add_argument("--pieces", type=int, default=1,
                     help="N > 1: parts per rank; each part's outputs are gathered while the "
                          "next part computes (1 = one shard per rank, gathered after it; "
