@@ -21,7 +21,11 @@
 //                                          shared memory, B MN-major (x rows s)
 // with W[l, s] = cb[l, s] exp(dA[l] - dA[s]) dt[s] for s <= l (< Q), else 0.
 // The cb rows of a key block land in shared memory and are turned into W in
-// place; cb / W and x blocks are triple-buffered (the third cb / W buffer is
+// place.  For bf16 on the tensor-copy path, when the tile's decay range
+// allows it, the decay is split instead: the x rows are scaled by
+// exp(ref - dA[s]) dt[s], cb enters the MMA as loaded (masked only in the
+// blocks that reach the diagonal) and row l of D2 is multiplied by
+// exp(dA[l] - ref) in the epilogue.  cb / W and x blocks are triple-buffered (the third cb / W buffer is
 // the C tile once the history MMA has read it) and requested two blocks
 // ahead.  Loads: with chunk length, d_head and d_state multiples of 64 the C
 // tile, x and cb blocks are tensor copies (one thread, mbarrier completion),
@@ -79,8 +83,9 @@ struct SsdLayout {
     // build reads them as float4).
     da = up1k(x + 3 * x_stride);
     dt = da + ((Q * 4 + 15) & ~15);
-    rng = dt + ((Q * 4 + 15) & ~15);  // per 64-key block: min, max of dA (2 x 16 floats)
-    bar = up1k(rng + 2 * 16 * 4);
+    // per 64-key block: min, max of dA, and 1.0f if its dA and dt are all finite (3 x 16 floats)
+    rng = dt + ((Q * 4 + 15) & ~15);
+    bar = up1k(rng + 3 * 16 * 4);
     bytes = bar + 64;
   }
   // cb / W block buffer i (0, 1: dedicated; 2: the C tile).
@@ -383,16 +388,19 @@ __global__ void __launch_bounds__(kSsdThreads, 2)
     mma_commit(&bars->d1_done);
   }
   {
-    // min / max of dA over each 64-key block (warp w: blocks w, w + 8, ...)
+    // min / max of dA over each 64-key block (warp w: blocks w, w + 8, ...),
+    // and whether every dA and dt of the block is finite
     float* rng = reinterpret_cast<float*>(sm + L.rng);
     const int lane = tid & 31;
     for (int jb = warp; jb * kSsdKBlk < Q; jb += kSsdThreads / 32) {
       float mn = INFINITY, mx = -INFINITY;
+      bool fin = true;
       for (int k = lane; k < kSsdKBlk; k += 32) {
         const int s = jb * kSsdKBlk + k;
         if (s < Q) {
           mn = fminf(mn, sdA[s]);
           mx = fmaxf(mx, sdA[s]);
+          fin = fin && fabsf(sdA[s]) < INFINITY && fabsf(sdt[s]) < INFINITY;
         }
       }
 #pragma unroll
@@ -400,13 +408,45 @@ __global__ void __launch_bounds__(kSsdThreads, 2)
         mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
       }
+      fin = __all_sync(0xffffffffu, fin);
       if (lane == 0) {
         rng[jb] = mn;
         rng[16 + jb] = mx;
+        rng[32 + jb] = fin ? 1.0f : 0.0f;
       }
     }
   }
   __syncthreads();
+
+  // Scaled-x form (16-bit type bf16, tensor-copy path): with one reference
+  // ref for the whole tile, exp(dA_l - dA_s) dt_s = exp(dA_l - ref) *
+  // (exp(ref - dA_s) dt_s).  The key factor scales the x rows of each block
+  // in place, the row factor multiplies row l of D2 in the epilogue, and cb
+  // feeds the MMA as loaded: only the blocks that reach the diagonal are
+  // touched, to zero their keys s > l.  ref = max(lo, hi - 100) with lo the
+  // smallest dA over the tile's keys and hi the largest over its rows (log2
+  // units), taken when every dA / dt of those keys is finite and hi - lo <=
+  // 128: then the row factor lies in [2^-28, 2^100] and the key factor
+  // amplifies x dt by at most 2^28.  A key factor that underflows belongs to
+  // an entry whose true decay is below 2^(100-126) for every row of the tile,
+  // invisible next to the 16-bit terms of the row's own keys.  Otherwise
+  // (and for fp16, whose range is too small for the scaled rows) the per-block
+  // W build below.
+  bool xfact = false;
+  float xref = 0.0f;
+  if constexpr (kTma && kBf16) {
+    const float* rng = reinterpret_cast<const float*>(sm + L.rng);
+    const int r0 = l0 / kSsdKBlk, r1 = min(r0 + 1, (Q - 1) / kSsdKBlk);
+    const float hi = fmaxf(rng[16 + r0], rng[16 + r1]);
+    float lo = rng[0];
+    bool fin = rng[32] != 0.0f;
+    for (int j = 1; j < nblk; ++j) {
+      lo = fminf(lo, rng[j]);
+      fin = fin && rng[32 + j] != 0.0f;
+    }
+    xfact = fin && hi - lo <= 128.0f;
+    xref = fmaxf(lo, hi - 100.0f);
+  }
 
   auto unpack2 = [](uint32_t u) -> float2 {  // a 16-bit pair -> two floats
     if constexpr (kBf16) {
@@ -493,6 +533,54 @@ __global__ void __launch_bounds__(kSsdThreads, 2)
       *slot = make_uint4(pk[0], pk[1], pk[2], pk[3]);
     }
   };
+  // Scaled-x form: x rows s of key block j times exp(ref - dA_s) dt_s, in
+  // place in buffer j % 3 (64 rows of P / 8 16-byte units, the layout the
+  // tensor copy wrote: 64-column chunks of [64][128 B], 128-byte swizzle).
+  auto scale_x = [&](int j) {
+    uint8_t* xb = sm + L.x + (j % 3) * L.x_stride;
+    const int upr = P / 8;
+    for (int i = tid; i < kSsdKBlk * upr; i += kSsdThreads) {
+      const int r = static_cast<int>(p.div_x.div(i)), u = i - r * upr;
+      const int s = j * kSsdKBlk + r;  // < Q: blocks never cross the chunk end here
+      const float f = ex2(xref - sdA[s]) * sdt[s];
+      uint4* slot = reinterpret_cast<uint4*>(xb + (u >> 3) * (kSsdKBlk * 128) + ssd_swz(r, u & 7));
+      uint4 v = *slot;
+      uint32_t* w = reinterpret_cast<uint32_t*>(&v);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 a = fmul2(unpack2(w[q]), make_float2(f, f));
+        w[q] = pack16<T>(a.x, a.y);
+      }
+      *slot = v;
+    }
+  };
+  // Scaled-x form, a block that reaches the diagonal: cb[l, s] -> 0 for keys
+  // s > l (packets wholly above the diagonal, and the tail of the packet the
+  // diagonal crosses).  Rows past the chunk arrived zero-filled.
+  auto mask_cb = [&](int j) {
+    const int sc = j * kSsdKBlk + cpk * 8;
+    uint8_t* wb = sm + L.wbuf(j % 3);
+#pragma unroll
+    for (int it = 0; it < kSsdRows / kSsdRowGroups; ++it) {
+      const int r = rg + kSsdRowGroups * it;
+      const int l = l0 + r;
+      if (sc + 7 <= l) continue;  // every key of the packet is visible
+      uint4* slot = reinterpret_cast<uint4*>(wb + ssd_swz(r, cpk));
+      if (sc > l) {
+        *slot = make_uint4(0u, 0u, 0u, 0u);
+        continue;
+      }
+      const int keep = l - sc + 1;  // keys sc .. l stay: 1 to 7 elements
+      uint4 v = *slot;
+      uint32_t* w = reinterpret_cast<uint32_t*>(&v);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {  // element 2q is the low half of word q
+        if (2 * q >= keep) w[q] = 0u;
+        else if (2 * q + 1 >= keep) w[q] &= 0x0000ffffu;
+      }
+      *slot = v;
+    }
+  };
 
   int issued = 0;  // key blocks whose MMAs were issued
   for (int j = 0; j < nblk; ++j) {
@@ -504,7 +592,14 @@ __global__ void __launch_bounds__(kSsdThreads, 2)
       if (j + 1 < nblk) cp_async_wait_prev();
       else cp_async_wait_all();
     }
-    if (okj) build_w(j);
+    if (okj) {
+      if (xfact) {
+        scale_x(j);
+        if (j * kSsdKBlk + kSsdKBlk - 1 > l0) mask_cb(j);
+      } else {
+        build_w(j);
+      }
+    }
     fence_proxy_async_smem();
     tc_fence_before();
     // Uniform: every thread leaves the loop here or none does.
@@ -575,6 +670,8 @@ __global__ void __launch_bounds__(kSsdThreads, 2)
     const int l = l0 + r;
     const uint32_t lane = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const float eh = l < Q ? ex2(sdA[l]) : 0.0f;
+    // Scaled-x form: D2 row l still carries exp(ref - dA_s) for its keys.
+    const float rfl = (xfact && l < Q) ? ex2(sdA[l] - xref) : 1.0f;
     const int U = P / 4;                            // units per row
     if (kTma && Q % kSsdRows == 0) {
       // Staged as 32-column (128-byte) slabs [128 rows][32] fp32 with the
@@ -591,10 +688,10 @@ __global__ void __launch_bounds__(kSsdThreads, 2)
 #pragma unroll
         for (int u = 0; u < 8; ++u)
           *reinterpret_cast<float4*>(slab + ((u ^ (r & 7)) << 4)) =
-              make_float4(fmaf(eh, __uint_as_float(x1[4 * u]), __uint_as_float(x2[4 * u])),
-                          fmaf(eh, __uint_as_float(x1[4 * u + 1]), __uint_as_float(x2[4 * u + 1])),
-                          fmaf(eh, __uint_as_float(x1[4 * u + 2]), __uint_as_float(x2[4 * u + 2])),
-                          fmaf(eh, __uint_as_float(x1[4 * u + 3]), __uint_as_float(x2[4 * u + 3])));
+              make_float4(fmaf(eh, __uint_as_float(x1[4 * u]), rfl * __uint_as_float(x2[4 * u])),
+                          fmaf(eh, __uint_as_float(x1[4 * u + 1]), rfl * __uint_as_float(x2[4 * u + 1])),
+                          fmaf(eh, __uint_as_float(x1[4 * u + 2]), rfl * __uint_as_float(x2[4 * u + 2])),
+                          fmaf(eh, __uint_as_float(x1[4 * u + 3]), rfl * __uint_as_float(x2[4 * u + 3])));
       }
       fence_proxy_async_smem();
       __syncthreads();
@@ -618,10 +715,10 @@ __global__ void __launch_bounds__(kSsdThreads, 2)
         const int u = (c0 + i) >> 2;
         const int us = (u & ~smask) | ((u ^ r) & smask);
         *reinterpret_cast<float4*>(stg + r * P + us * 4) =
-            make_float4(fmaf(eh, __uint_as_float(x1[i]), __uint_as_float(x2[i])),
-                        fmaf(eh, __uint_as_float(x1[i + 1]), __uint_as_float(x2[i + 1])),
-                        fmaf(eh, __uint_as_float(x1[i + 2]), __uint_as_float(x2[i + 2])),
-                        fmaf(eh, __uint_as_float(x1[i + 3]), __uint_as_float(x2[i + 3])));
+            make_float4(fmaf(eh, __uint_as_float(x1[i]), rfl * __uint_as_float(x2[i])),
+                        fmaf(eh, __uint_as_float(x1[i + 1]), rfl * __uint_as_float(x2[i + 1])),
+                        fmaf(eh, __uint_as_float(x1[i + 2]), rfl * __uint_as_float(x2[i + 2])),
+                        fmaf(eh, __uint_as_float(x1[i + 3]), rfl * __uint_as_float(x2[i + 3])));
       }
     }
     __syncthreads();
