@@ -62,36 +62,67 @@ __device__ __forceinline__ uint32_t ssd_swz(int r, int u) {
   return static_cast<uint32_t>(r * 128 + ((u ^ (r & 7)) << 4));
 }
 
+constexpr int kSsdBarBytes = 128;  // the SsdBars block at the end of the layout
+
 // Shared-memory layout, sized per call (offsets in bytes from a 1 KB-aligned
 // base, every tile 1 KB aligned): C [128][nc64] and prev [P][nc64] K-major
-// (nc64 = d_state rounded up to 64-column chunks), two cb / W blocks
-// [128][64], three x blocks [64][pc64] MN-major (pc64 = d_head rounded up to
-// 64), dA and dt of the chunk, the barriers.  The third cb / W block lives in
-// the C tile once the history MMA has read it.
+// (nc64 = d_state rounded up to 64-column chunks) for the history MMA, three
+// key-block buffers, each a cb / W block [128][64] and an x block [64][pc64]
+// MN-major (pc64 = d_head rounded up to 64), dA (fp32) and dt (the 16-bit
+// type) of the chunk, the per-block dA ranges, the barriers.
+//   ring = false (cp.async path): two dedicated cb / W blocks, three dedicated
+//     x blocks; the third cb / W block lives in the C tile once the history
+//     MMA has read it.
+//   ring = true (tensor-copy path): buffer 0 is dedicated; buffers 1 and 2
+//     (a cb block and its x block each) reuse the C / prev region once the
+//     history MMA has read it, which keeps the bf16 / fp16 d_head 64,
+//     d_state 128, chunk 256 case at 76.6 KB, three CTAs per SM.
 struct SsdLayout {
   int c, prev, w, x, da, dt, rng, bar, bytes;
-  int x_stride;  // bytes of one x block
+  int x_stride;  // ring = false: bytes of one x block
+  int slot;      // ring = true: bytes of one buffer (cb block + x block)
+  int ring0;     // ring = true: offset of buffer 0
+  bool ring;
   __host__ __device__ static int up1k(int v) { return (v + 1023) & ~1023; }
-  __host__ __device__ SsdLayout(int P, int N, int Q) {
+  __host__ __device__ SsdLayout(int P, int N, int Q, bool ring_) : ring(ring_) {
     const int nc64 = ((N + 63) / 64) * 64, pc64 = ((P + 63) / 64) * 64;
+    constexpr int kCb = kSsdRows * kSsdKBlk * 2;
     c = 0;
     prev = up1k(c + kSsdRows * nc64 * 2);
-    w = up1k(prev + P * nc64 * 2);
-    x = w + 2 * kSsdRows * kSsdKBlk * 2;
+    const int hist_end = up1k(prev + P * nc64 * 2);
     x_stride = kSsdKBlk * pc64 * 2;
-    // dA and dt of the chunk, each starting on a 16-byte boundary (the W
-    // build reads them as float4).
-    da = up1k(x + 3 * x_stride);
+    slot = kCb + x_stride;
+    int end;
+    if (ring) {
+      ring0 = hist_end > 2 * slot ? hist_end : 2 * slot;  // buffers 1, 2 below it
+      w = x = -1;
+      end = ring0 + slot;
+    } else {
+      ring0 = -1;
+      w = hist_end;
+      x = w + 2 * kCb;
+      end = x + 3 * x_stride;
+    }
+    // dA (fp32) and dt (16-bit) of the chunk, each starting on a 16-byte
+    // boundary (the W build reads 8 keys of each at once).
+    da = end;
     dt = da + ((Q * 4 + 15) & ~15);
     // per 64-key block: min, max of dA, and 1.0f if its dA and dt are all finite (3 x 16 floats)
-    rng = dt + ((Q * 4 + 15) & ~15);
-    bar = up1k(rng + 3 * 16 * 4);
-    bytes = bar + 64;
+    rng = dt + ((Q * 2 + 15) & ~15);
+    bar = rng + 3 * 16 * 4;
+    bytes = bar + kSsdBarBytes;
   }
-  // cb / W block buffer i (0, 1: dedicated; 2: the C tile).
-  __host__ __device__ int wbuf(int i) const {
+  // cb / W block of buffer i.  ring = false: 0, 1 dedicated, 2 the C tile.
+  __host__ __device__ int cbuf(int i) const {
+    if (ring) return i == 0 ? ring0 : (i - 1) * slot;
     return i == 2 ? c : w + i * (kSsdRows * kSsdKBlk * 2);
   }
+  // x block of buffer i.
+  __host__ __device__ int xbuf(int i) const {
+    return ring ? cbuf(i) + kSsdRows * kSsdKBlk * 2 : x + i * x_stride;
+  }
+  // Output staging after the last MMA: a region of at least 128 x P fp32.
+  __host__ __device__ int stage() const { return ring ? 0 : w; }
 };
 
 struct SsdBars {
@@ -103,6 +134,7 @@ struct SsdBars {
   uint32_t tmem_base;
   int abort_flag;
 };
+static_assert(sizeof(SsdBars) <= kSsdBarBytes, "SsdBars outgrew its layout slot");
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
@@ -156,19 +188,19 @@ struct SsdParams {
 // With kTma and a chunk length that is a multiple of 128 (no row tile
 // reaches into the next chunk) the output leaves by tensor stores too.
 template <typename T, bool kTma>
-__global__ void __launch_bounds__(kSsdThreads, 2)
+__global__ void __launch_bounds__(kSsdThreads, kTma ? 3 : 2)
     ssd_chunk_scan(const SsdParams p, const __grid_constant__ CUtensorMap tm_x,
                    const __grid_constant__ CUtensorMap tm_c,
                    const __grid_constant__ CUtensorMap tm_cb,
                    const __grid_constant__ CUtensorMap tm_out) {
-  const SsdLayout L(p.P, p.N, p.Q);
+  const SsdLayout L(p.P, p.N, p.Q, kTma);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   SsdBars* bars = reinterpret_cast<SsdBars*>(sm + L.bar);
   volatile int* abort_flag = &bars->abort_flag;
   float* sdA = reinterpret_cast<float*>(sm + L.da);
-  float* sdt = reinterpret_cast<float*>(sm + L.dt);
+  T* sdt = reinterpret_cast<T*>(sm + L.dt);
   const uint32_t sb = smem_u32(sm);
   const int tid = threadIdx.x, warp = tid >> 5;
 
@@ -215,10 +247,12 @@ __global__ void __launch_bounds__(kSsdThreads, 2)
 
   // ---- prologue: every global load of the CTA's first two blocks in flight
   // at once (prev and dA / dt into registers, C, x and cb by cp.async).
-  float4 va[8], vb[8];  // this thread's first eight prev packets (fp32)
+  // prev packets per thread and round: four at three CTAs per SM (80 registers)
+  constexpr int kPrevPer = kTma ? 4 : 8;
+  float4 va[kPrevPer], vb[kPrevPer];  // this thread's prev packets of a round (fp32)
   auto load_prev = [&](int base) {
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
+    for (int k = 0; k < kPrevPer; ++k) {
       const int i = base + k * kSsdThreads + tid;
       va[k] = vb[k] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       if (i < ptotal) {
@@ -233,7 +267,7 @@ __global__ void __launch_bounds__(kSsdThreads, 2)
   };
   auto store_prev = [&](int base) {  // -> dtype, K-major [p][n]
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
+    for (int k = 0; k < kPrevPer; ++k) {
       const int i = base + k * kSsdThreads + tid;
       if (i < ptotal) {
         const int r = static_cast<int>(p.div_c.div(i)), n = (i - r * pupr) * 8;
@@ -249,13 +283,14 @@ __global__ void __launch_bounds__(kSsdThreads, 2)
   };
   load_prev(0);
   constexpr int kMaxQPerThread = kSsdMaxQ / kSsdThreads;
-  float rdA[kMaxQPerThread], rdt[kMaxQPerThread];
+  float rdA[kMaxQPerThread];
+  T rdt[kMaxQPerThread];
 #pragma unroll
   for (int k = 0; k < kMaxQPerThread; ++k) {
     const int i = tid + k * kSsdThreads;
     if (i < Q) {
       rdA[k] = p.dA[hc * Q + i];
-      rdt[k] = Cvt<T>::to_f(static_cast<const T*>(p.dt)[hc * Q + i]);
+      rdt[k] = static_cast<const T*>(p.dt)[hc * Q + i];
     }
   }
 
@@ -266,7 +301,7 @@ __global__ void __launch_bounds__(kSsdThreads, 2)
   const bool cbvec = (Q & 7) == 0;
   auto issue_cb = [&](int j) {  // cb rows of key block j -> cb / W buffer j % 3
     const int sc = j * kSsdKBlk + cpk * 8;
-    uint8_t* dst = sm + L.wbuf(j % 3);
+    uint8_t* dst = sm + L.cbuf(j % 3);
 #pragma unroll
     for (int it = 0; it < kSsdRows / kSsdRowGroups; ++it) {
       const int r = rg + kSsdRowGroups * it;
@@ -276,7 +311,7 @@ __global__ void __launch_bounds__(kSsdThreads, 2)
       const bool ok = l < Q && sc <= l && sc < Q;
       const T* row = cbg + static_cast<int64_t>(ok ? l : 0) * Q + (ok ? sc : 0);
       if (cbvec) {
-        cp_async16(sb + L.wbuf(j % 3) + ssd_swz(r, cpk), row, ok);
+        cp_async16(sb + L.cbuf(j % 3) + ssd_swz(r, cpk), row, ok);
       } else {
         uint4 v = make_uint4(0u, 0u, 0u, 0u);
         if (ok) {
@@ -295,7 +330,7 @@ __global__ void __launch_bounds__(kSsdThreads, 2)
       const int s = s0 + r, pc = u * 8;
       const bool ok = s < Q;
       const T* src = xg + ((static_cast<int64_t>(b) * S + c * Q + (ok ? s : 0)) * p.H + h) * P + pc;
-      cp_async16(sb + L.x + (j % 3) * L.x_stride + (pc >> 6) * (kSsdKBlk * 128) +
+      cp_async16(sb + L.xbuf(j % 3) + (pc >> 6) * (kSsdKBlk * 128) +
                      ssd_swz(r, (pc & 63) >> 3),
                  src, ok);
     }
@@ -308,9 +343,9 @@ __global__ void __launch_bounds__(kSsdThreads, 2)
     mbar_arrive_expect_tx(&bars->full[i],
                           static_cast<uint32_t>(P * kSsdKBlk * 2 + kSsdRows * kSsdKBlk * 2));
     for (int pc = 0; pc < P; pc += 64)
-      tma_load_4d(sm + L.x + i * L.x_stride + (pc >> 6) * (kSsdKBlk * 128), &tm_x,
+      tma_load_4d(sm + L.xbuf(i) + (pc >> 6) * (kSsdKBlk * 128), &tm_x,
                   &bars->full[i], pc, h, c * Q + j * kSsdKBlk, b);
-    tma_load_3d(sm + L.wbuf(i), &tm_cb, &bars->full[i], j * kSsdKBlk, l0, bcg);
+    tma_load_3d(sm + L.cbuf(i), &tm_cb, &bars->full[i], j * kSsdKBlk, l0, bcg);
     armed[i] = j;
   };
   if constexpr (kTma) {
@@ -322,8 +357,7 @@ __global__ void __launch_bounds__(kSsdThreads, 2)
       for (int n0 = 0; n0 < N; n0 += 64)
         tma_load_4d(sm + L.c + (n0 >> 6) * (kSsdRows * 128), &tm_c, &bars->c_full, n0, g,
                     c * Q + l0, b);
-      tma_blk(0);
-      if (nblk > 1) tma_blk(1);
+      tma_blk(0);  // buffers 1 and 2 hold C / prev until the history MMA has read them
     }
   } else {
     const T* Cg = static_cast<const T*>(p.C);
@@ -355,7 +389,7 @@ __global__ void __launch_bounds__(kSsdThreads, 2)
     }
   }
   store_prev(0);
-  for (int base = 8 * kSsdThreads; base < ptotal; base += 8 * kSsdThreads) {
+  for (int base = kPrevPer * kSsdThreads; base < ptotal; base += kPrevPer * kSsdThreads) {
     load_prev(base);  // shapes with more than 8 prev packets per thread
     store_prev(base);
   }
@@ -400,7 +434,7 @@ __global__ void __launch_bounds__(kSsdThreads, 2)
         if (s < Q) {
           mn = fminf(mn, sdA[s]);
           mx = fmaxf(mx, sdA[s]);
-          fin = fin && fabsf(sdA[s]) < INFINITY && fabsf(sdt[s]) < INFINITY;
+          fin = fin && fabsf(sdA[s]) < INFINITY && fabsf(Cvt<T>::to_f(sdt[s])) < INFINITY;
         }
       }
 #pragma unroll
@@ -457,7 +491,7 @@ __global__ void __launch_bounds__(kSsdThreads, 2)
   };
   auto build_w = [&](int j) {  // cb block j -> W, in place in buffer j % 3
     const int s0 = j * kSsdKBlk, sc = s0 + cpk * 8;
-    uint8_t* wb = sm + L.wbuf(j % 3);
+    uint8_t* wb = sm + L.cbuf(j % 3);
     // exp(dA_l - dA_s) = exp(dA_l - ref) exp(ref - dA_s) with ref = dA[s0]
     // when neither factor can overflow: the block's keys lie within 2^100 of
     // ref (ref - min dA_s <= 100 in log2 units) and no row of the tile lies
@@ -473,22 +507,22 @@ __global__ void __launch_bounds__(kSsdThreads, 2)
     if (sc + 8 <= Q) {  // 32-byte aligned: sc is a multiple of 8
       const float4 a0 = *reinterpret_cast<const float4*>(sdA + sc);
       const float4 a1 = *reinterpret_cast<const float4*>(sdA + sc + 4);
-      const float4 t0 = *reinterpret_cast<const float4*>(sdt + sc);
-      const float4 t1 = *reinterpret_cast<const float4*>(sdt + sc + 4);
+      const uint4 tv = *reinterpret_cast<const uint4*>(sdt + sc);  // 16-byte aligned
       das[0] = make_float2(a0.x, a0.y);
       das[1] = make_float2(a0.z, a0.w);
       das[2] = make_float2(a1.x, a1.y);
       das[3] = make_float2(a1.z, a1.w);
-      dts[0] = make_float2(t0.x, t0.y);
-      dts[1] = make_float2(t0.z, t0.w);
-      dts[2] = make_float2(t1.x, t1.y);
-      dts[3] = make_float2(t1.z, t1.w);
+      dts[0] = unpack2(tv.x);
+      dts[1] = unpack2(tv.y);
+      dts[2] = unpack2(tv.z);
+      dts[3] = unpack2(tv.w);
     } else {
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         const int s = sc + 2 * q;
         das[q] = make_float2(s < Q ? sdA[s] : ref, s + 1 < Q ? sdA[s + 1] : ref);
-        dts[q] = make_float2(s < Q ? sdt[s] : 0.0f, s + 1 < Q ? sdt[s + 1] : 0.0f);
+        dts[q] = make_float2(s < Q ? Cvt<T>::to_f(sdt[s]) : 0.0f,
+                             s + 1 < Q ? Cvt<T>::to_f(sdt[s + 1]) : 0.0f);
       }
     }
     if (fact) {  // exp(ref - dA_s) dt_s
@@ -537,12 +571,12 @@ __global__ void __launch_bounds__(kSsdThreads, 2)
   // place in buffer j % 3 (64 rows of P / 8 16-byte units, the layout the
   // tensor copy wrote: 64-column chunks of [64][128 B], 128-byte swizzle).
   auto scale_x = [&](int j) {
-    uint8_t* xb = sm + L.x + (j % 3) * L.x_stride;
+    uint8_t* xb = sm + L.xbuf(j % 3);
     const int upr = P / 8;
     for (int i = tid; i < kSsdKBlk * upr; i += kSsdThreads) {
       const int r = static_cast<int>(p.div_x.div(i)), u = i - r * upr;
       const int s = j * kSsdKBlk + r;  // < Q: blocks never cross the chunk end here
-      const float f = ex2(xref - sdA[s]) * sdt[s];
+      const float f = ex2(xref - sdA[s]) * Cvt<T>::to_f(sdt[s]);
       uint4* slot = reinterpret_cast<uint4*>(xb + (u >> 3) * (kSsdKBlk * 128) + ssd_swz(r, u & 7));
       uint4 v = *slot;
       uint32_t* w = reinterpret_cast<uint32_t*>(&v);
@@ -559,7 +593,7 @@ __global__ void __launch_bounds__(kSsdThreads, 2)
   // diagonal crosses).  Rows past the chunk arrived zero-filled.
   auto mask_cb = [&](int j) {
     const int sc = j * kSsdKBlk + cpk * 8;
-    uint8_t* wb = sm + L.wbuf(j % 3);
+    uint8_t* wb = sm + L.cbuf(j % 3);
 #pragma unroll
     for (int it = 0; it < kSsdRows / kSsdRowGroups; ++it) {
       const int r = rg + kSsdRowGroups * it;
@@ -600,6 +634,16 @@ __global__ void __launch_bounds__(kSsdThreads, 2)
         build_w(j);
       }
     }
+    if constexpr (kTma) {
+      // Buffers 1 and 2 reuse the C / prev region: blocks 1 and 2 are requested
+      // once the history MMA has read it, before this iteration's barrier, so
+      // a failed wait reaches every thread before any waits for block 1.
+      if (j == 0 && tid == 0 && ok) {
+        ok = mbar_wait(&bars->d1_done, 0, p.err, abort_flag);
+        if (ok && nblk > 1) tma_blk(1);
+        if (ok && nblk > 2) tma_blk(2);
+      }
+    }
     fence_proxy_async_smem();
     tc_fence_before();
     // Uniform: every thread leaves the loop here or none does.
@@ -609,8 +653,8 @@ __global__ void __launch_bounds__(kSsdThreads, 2)
     }
     tc_fence_after();
     if (tid == 0) {
-      const uint64_t a = smem_desc(sb + L.wbuf(j % 3), 16, 1024);
-      const uint64_t bd = smem_desc(sb + L.x + (j % 3) * L.x_stride, kSsdKBlk * 128, 1024);
+      const uint64_t a = smem_desc(sb + L.cbuf(j % 3), 16, 1024);
+      const uint64_t bd = smem_desc(sb + L.xbuf(j % 3), kSsdKBlk * 128, 1024);
 #pragma unroll
       for (int kk = 0; kk < kSsdKBlk / 16; ++kk)
         mma_f16_ss(t_d2, desc_advance(a, kk * 32), desc_advance(bd, kk * 16 * 128), id_kmn,
@@ -620,14 +664,13 @@ __global__ void __launch_bounds__(kSsdThreads, 2)
     issued = j + 1;
     if (j + 2 < nblk) {
       // Block j + 2 goes to the buffers block j - 1 read (for j = 0: the
-      // third cb buffer, the C tile, which the history MMA read).
+      // third cb buffer, the C tile, which the history MMA read; on the
+      // tensor-copy path block 2 was requested with block 1 above).
       if constexpr (kTma) {
-        if (tid == 0) {
+        if (tid == 0 && j >= 1) {
           // A failed wait shows at the next iteration's barrier, before any
           // thread waits for the block not issued here.
-          ok = j >= 1 ? mbar_wait(&bars->blk_done[(j - 1) % 3], ((j - 1) / 3) & 1, p.err,
-                                  abort_flag)
-                      : mbar_wait(&bars->d1_done, 0, p.err, abort_flag);
+          ok = mbar_wait(&bars->blk_done[(j - 1) % 3], ((j - 1) / 3) & 1, p.err, abort_flag);
           if (ok) tma_blk(j + 2);
         }
       } else {
@@ -677,7 +720,7 @@ __global__ void __launch_bounds__(kSsdThreads, 2)
       // Staged as 32-column (128-byte) slabs [128 rows][32] fp32 with the
       // 128-byte swizzle (16-byte unit u of row r at u ^ (r % 8)), each slab
       // written by one tensor store.
-      uint8_t* stg = sm + L.w;
+      uint8_t* stg = sm + L.stage();
       for (int c0 = 32 * (warp >> 2); c0 < P; c0 += 64) {
         uint32_t x1[32], x2[32];
         tmem_ld32(t_d1 + lane + c0, x1);
@@ -703,7 +746,7 @@ __global__ void __launch_bounds__(kSsdThreads, 2)
       }
     } else {
     const int smask = (U & 7) == 0 ? 7 : 3;
-    float* stg = reinterpret_cast<float*>(sm + L.w);
+    float* stg = reinterpret_cast<float*>(sm + L.stage());
     for (int c0 = 32 * (warp >> 2); c0 < P; c0 += 64) {
       uint32_t x1[32], x2[32];
       tmem_ld32(t_d1 + lane + c0, x1);
@@ -778,7 +821,7 @@ int launch_ssd(const SsdParams& p, cudaStream_t s) {
     }
   }
   auto k = tma ? ssd_chunk_scan<T, true> : ssd_chunk_scan<T, false>;
-  const int smem = SsdLayout(p.P, p.N, p.Q).bytes + 1024;  // + room to align the base
+  const int smem = SsdLayout(p.P, p.N, p.Q, tma).bytes + 1024;  // + room to align the base
   if (smem > 232448) return TILEOPS_EBADSHAPE;
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return TILEOPS_ELAUNCH;
