@@ -1,6 +1,7 @@
 // Library-level entry points of the C ABI: version, status strings, the
 // device-side error flag of bounded waits, and the cached SM count.
 #include <mutex>
+#include <vector>
 
 #include "common.cuh"
 #include "device_error.cuh"
@@ -28,10 +29,11 @@ __device__ int g_device_error = 0;
 
 int* device_error_ptr() {
   static std::mutex mu;
-  static int* cached[64] = {nullptr};
+  static std::vector<int*> cached;  // by device index
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return nullptr;
   std::lock_guard<std::mutex> lock(mu);
+  if (cached.size() <= static_cast<size_t>(dev)) cached.resize(static_cast<size_t>(dev) + 1, nullptr);
   if (!cached[dev]) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;

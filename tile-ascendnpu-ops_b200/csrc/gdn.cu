@@ -47,6 +47,7 @@
 // head h is workspace unit H base_n + h nc_n + c (for a uniform batch the
 // (b, h, chunk) order, consecutive units = consecutive chunks of one head).
 #include <mutex>
+#include <vector>
 
 #include "common.cuh"
 #include "sm100.cuh"
@@ -1534,18 +1535,18 @@ extern "C" int tileops_gdn_prefill_varlen_fwd(const void* q, const void* k, cons
 //    and the device error word that the kernels' bounded waits write -- with
 //    cudaGetSymbolAddress, which may load the module lazily; make that first
 //    call outside any stream capture.  Later calls only read the cached
-//    addresses.  Devices are cached by index up to 63; a higher device index
-//    is refused with TILEOPS_ELAUNCH.
+//    addresses (one entry per device index, any index).
 constexpr size_t kGdnStaticScratchBytes = static_cast<size_t>(16) << 20;
 static __device__ __align__(256) unsigned char g_gdn_static_scratch[kGdnStaticScratchBytes];
 
 namespace {
 void* gdn_static_scratch_ptr() {
   static std::mutex mu;
-  static void* cached[64] = {nullptr};
+  static std::vector<void*> cached;  // by device index
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return nullptr;
   std::lock_guard<std::mutex> lock(mu);
+  if (cached.size() <= static_cast<size_t>(dev)) cached.resize(static_cast<size_t>(dev) + 1, nullptr);
   if (!cached[dev]) {
     // Resolve the error word too, so one first call covers every lookup.
     if (!tileops::device_error_ptr()) return nullptr;
