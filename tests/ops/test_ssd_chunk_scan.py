@@ -95,6 +95,31 @@ def test_odd_chunk_and_state_sizes(Q, N):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("key", [100, 64, 255])
+def test_nan_decay_stays_in_its_rows(key):
+    """A NaN in dA at key s of one (chunk, head) makes exactly rows l >= s of
+    that chunk and head NaN, as the golden's masked decay does; rows before it
+    and every other chunk / head keep their values.  bf16 with chunk 256 takes
+    the kernel's scaled-x decay form, whose finiteness check must send the
+    affected tiles to the per-block W build (a scaled x row of NaN would reach
+    the rows above the diagonal too); key 64 is the first key of a block."""
+    x, cb, dA, Cm, prev, dt = _inputs(1, 2, 256, 4, 64, 128, 1, torch.bfloat16, seed=50)
+    dA = dA.cpu()
+    dA[0, 1, 0, key] = float("nan")
+    dA = dA.cuda()
+    out = SSDChunkScanFwdOp()(x, cb, dA, Cm, prev, dt).cpu()
+    expect = ref.ssd_chunk_scan(x, cb, dA, Cm, prev, dt, 1)
+    nan_rows = torch.zeros(2 * 256, 4, dtype=torch.bool)
+    nan_rows[key:256, 1] = True  # chunk 0, head 1, rows l >= key
+    assert torch.equal(torch.isnan(expect).all(-1)[0], nan_rows)
+    assert torch.equal(torch.isnan(out), torch.isnan(expect))
+    keep = ~torch.isnan(expect)
+    diff = (out[keep] - expect[keep]).abs()
+    assert bool((diff <= _ATOL[torch.bfloat16] + _RTOL * expect[keep].abs()).all()), \
+        f"max_diff {diff.max().item():.3e}"
+
+
+@pytest.mark.gpu
 def test_deterministic():
     inp = _inputs(1, 4, 128, 8, 64, 64, 1, torch.bfloat16, seed=7)
     op = SSDChunkScanFwdOp()
