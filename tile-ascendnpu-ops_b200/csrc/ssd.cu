@@ -12,8 +12,9 @@
 // and kernels/mamba/ssd_chunk_scan/ssd_chunk_scan_kernel/perf_opt/
 // _ssd_chunk_scan_fwd_kernel.py:181 (golden at :123-178).
 //
-// One CTA (256 threads, two per SM) per (b, c, h, 128-row tile of the
-// chunk); row l0 + r of the tile is TMEM lane r.  Both terms are tcgen05 MMAs (M = 128,
+// One CTA (256 threads; three per SM on the tensor-copy path, two on the
+// cp.async path) per (b, c, h, 128-row tile of the chunk); row l0 + r of the
+// tile is TMEM lane r.  Both terms are tcgen05 MMAs (M = 128,
 // N = P, kind::f16, fp32 accumulators in TMEM):
 //   D1 = C_tile [128 x N] . prev^T        A K-major (C rows), B K-major (prev
 //                                          rows p, converted fp32 -> dtype)
