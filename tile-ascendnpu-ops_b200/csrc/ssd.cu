@@ -26,14 +26,15 @@
 // allows it, the decay is split instead: the x rows are scaled by
 // exp(ref - dA[s]) dt[s], cb enters the MMA as loaded (masked only in the
 // blocks that reach the diagonal) and row l of D2 is multiplied by
-// exp(dA[l] - ref) in the epilogue.  cb / W and x blocks are triple-buffered (the third cb / W buffer is
-// the C tile once the history MMA has read it) and requested two blocks
-// ahead.  Loads: with chunk length, d_head and d_state multiples of 64 the C
-// tile, x and cb blocks are tensor copies (one thread, mbarrier completion),
-// otherwise 16-byte cp.async from every thread (zero fill past the chunk /
-// past N).  Epilogue: out = exp(dA[l]) D1 + D2 from TMEM, staged in shared
-// memory and written by tensor stores (chunk length a multiple of 128) or by
-// row-wise vector stores.
+// exp(dA[l] - ref) in the epilogue.  cb / W and x blocks are triple-buffered
+// and requested two blocks ahead; buffers the history operands occupy are
+// reused once the history MMA has read them (SsdLayout).  Loads: with chunk
+// length, d_head and d_state multiples of 64 the C tile, x and cb blocks are
+// tensor copies (one thread, mbarrier completion), otherwise 16-byte cp.async
+// from every thread (zero fill past the chunk / past N).  Epilogue:
+// out = exp(dA[l]) D1 + r_l D2 from TMEM (r_l the row factor, 1 for the W
+// build), staged in shared memory and written by tensor stores (chunk length a
+// multiple of 128) or by row-wise vector stores.
 // Every mbarrier wait (sm100::mbar_wait) checks a 2 s limit between its
 // try_wait polls; a phase that completes late sets the device error flag, the
 // MMAs issued so far are drained and TMEM is freed before returning.
